@@ -1,0 +1,694 @@
+// FlashAttention forward for B200 (sm_100a): fp16 Q/K/V in [B, H, N, 64]
+// layout, fp32 accumulation, fp16 output, optional top-left causal mask.
+//
+// It replaces the sm_80-style production kernel of the reference
+// (csrc/tensorcore_attention.cu:2019-2727, launched from :2969-3123) with a
+// warp-specialized, persistent tcgen05 design:
+//
+//   warp 8      TMA producer: Q tiles of the current work item, then K_j/V_j
+//               tiles through a ring of swizzled shared-memory slots.
+//   warp 9      MMA issuer (one thread): S_t = Q_t K_j^T (SS form) and
+//               O_t += P_t V_j (P read straight from tensor memory, TS form).
+//               It also owns the tensor-memory allocation.
+//   warps 0-3   softmax for query tile 0 of the work item, one thread per row.
+//   warps 4-7   softmax for query tile 1 (ping-pong partner of tile 0).
+//   warps 10-11 idle (kept so the block is three whole warpgroups).
+//
+// A work item is one (batch*head, query-pair) unit: 256 query rows as two
+// 128-row tiles.  Tensor memory (512 columns) holds, per tile t,
+//   S_t  128 x 128 fp32   (columns   0 / 128)
+//   O_t  128 x  64 fp32   (columns 256 / 320)
+//   P_t  128 x 128 fp16   (columns 384 / 448, two halves per column)
+// so the MMA warp can compute S_t(j+1) while the softmax warps are still
+// turning S_t(j) into P_t(j).
+//
+// Online softmax follows the reference's tile update
+// (csrc/tensorcore_attention.cu:448-671): running row max m, running sum l,
+// p = exp(s*scale - m), O rescaled by exp(m_old - m_new).  The max used for
+// the exponent is only moved when the row max grows by more than 2^8 in the
+// exponent, which keeps every p <= 256 (exact in fp16) and skips most O
+// rescales; the final O / l is unchanged because both use the same max.
+//
+// Every wait is bounded in time.  A wait that runs out sets a bit in a device
+// status word, sets a shared abort flag that releases the other roles, and the
+// block drains its in-flight copies and frees tensor memory before returning.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "sm100_ptx.cuh"
+#include "../../include/fa_sm100.h"
+
+namespace fa {
+using namespace ptx;
+
+constexpr int kHeadDim = 64;
+constexpr int kBlockM = 128;   // query rows per tile
+constexpr int kBlockN = 128;   // key rows per tile
+constexpr int kKvSlots = 6;    // shared-memory ring of 16 KiB K/V tiles
+constexpr int kNumThreads = 384;
+constexpr uint32_t kTileBytes = kBlockM * kHeadDim * 2;  // 16 KiB, also a K/V tile
+
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemKV = kSmemQ + 2 * kTileBytes;
+constexpr uint32_t kSmemO = kSmemKV + kKvSlots * kTileBytes;
+constexpr uint32_t kSmemCtl = kSmemO + 2 * kTileBytes;
+constexpr uint32_t kSmemCtlBytes = 256;
+constexpr uint32_t kSmemBytes = kSmemCtl + kSmemCtlBytes + 1024;  // + alignment slack
+
+constexpr uint32_t kTmemCols = 512;
+__host__ __device__ constexpr uint32_t col_s(int t) { return t == 0 ? 0u : 128u; }
+__host__ __device__ constexpr uint32_t col_o(int t) { return t == 0 ? 256u : 320u; }
+__host__ __device__ constexpr uint32_t col_p(int t) { return t == 0 ? 384u : 448u; }
+
+// Status bits written by the kernel (OR-ed into the device status word).
+constexpr unsigned int kStatusTimeoutProducer = 1u << 0;
+constexpr unsigned int kStatusTimeoutMma = 1u << 1;
+constexpr unsigned int kStatusTimeoutSoftmax = 1u << 2;
+constexpr unsigned int kStatusTimeoutDrain = 1u << 3;
+constexpr unsigned int kStatusTimeoutSelftest = 1u << 4;
+
+struct SharedCtl {
+  uint64_t q_full, q_empty;
+  uint64_t kv_full[kKvSlots], kv_empty[kKvSlots];
+  uint64_t s_full[2], s_empty[2], p_full[2], o_done[2], o_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(SharedCtl) <= kSmemCtlBytes, "control block too large");
+
+struct FwdParams {
+  int n_q;          // query rows per (batch, head)
+  int n_k;          // key/value rows per (batch, head)
+  int bh;           // batch * heads
+  int causal;       // top-left aligned: key index > query index is masked
+  float scale_log2; // softmax scale * log2(e)
+  int n_qpairs;     // ceil(ceil(n_q / 128) / 2)
+  int n_items;      // bh * n_qpairs
+  unsigned int* status;
+  unsigned long long limit_ns;
+  float* dbg;       // optional: first item's first masked score tile (tests)
+};
+
+struct ItemShape {
+  int bh, qp, n_t[2], n_max, q0[2];
+};
+
+__device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
+  ItemShape s;
+  s.bh = item / p.n_qpairs;
+  const int r = item - s.bh * p.n_qpairs;
+  // Causal work grows with the query position: hand out the heaviest pairs of
+  // a head first so the static round-robin schedule ends balanced.
+  s.qp = p.causal ? (p.n_qpairs - 1 - r) : r;
+  const int nkv = (p.n_k + kBlockN - 1) / kBlockN;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    s.q0[t] = s.qp * 2 * kBlockM + t * kBlockM;
+    if (s.q0[t] >= p.n_q) {
+      s.n_t[t] = 0;
+    } else if (p.causal) {
+      const int diag = s.q0[t] / kBlockN + 1;  // tiles up to and including the diagonal
+      s.n_t[t] = diag < nkv ? diag : nkv;
+    } else {
+      s.n_t[t] = nkv;
+    }
+  }
+  s.n_max = s.n_t[0] > s.n_t[1] ? s.n_t[0] : s.n_t[1];
+  return s;
+}
+
+// ------------------------------------------------------------------ roles
+__device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
+                              const CUtensorMap* tm_q, const CUtensorMap* tm_k,
+                              const CUtensorMap* tm_v, uint32_t& ld_count, uint32_t& q_count) {
+  volatile int* abort_flag = &ctl->abort;
+  const uint32_t q_full = smem_u32(&ctl->q_full), q_empty = smem_u32(&ctl->q_empty);
+  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+    const ItemShape s = decode_item(item, p);
+    if (!mbar_wait(q_empty, (q_count & 1) ^ 1, abort_flag, p.status, kStatusTimeoutProducer,
+                   p.limit_ns))
+      return false;
+    const uint32_t nq = (s.n_t[1] > 0) ? 2 : 1;
+    mbar_arrive_expect_tx(q_full, nq * kTileBytes);
+    tma_load_3d(smem_base + kSmemQ, tm_q, q_full, 0, s.q0[0], s.bh);
+    if (nq == 2) tma_load_3d(smem_base + kSmemQ + kTileBytes, tm_q, q_full, 0, s.q0[1], s.bh);
+    ++q_count;
+    for (int j = 0; j < s.n_max; ++j) {
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t slot = ld_count % kKvSlots;
+        const uint32_t phase = (ld_count / kKvSlots) & 1;
+        if (!mbar_wait(smem_u32(&ctl->kv_empty[slot]), phase ^ 1, abort_flag, p.status,
+                       kStatusTimeoutProducer, p.limit_ns))
+          return false;
+        const uint32_t full = smem_u32(&ctl->kv_full[slot]);
+        mbar_arrive_expect_tx(full, kTileBytes);
+        tma_load_3d(smem_base + kSmemKV + slot * kTileBytes, which ? tm_v : tm_k, full, 0,
+                    j * kBlockN, s.bh);
+        ++ld_count;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
+                         uint32_t tmem) {
+  volatile int* abort_flag = &ctl->abort;
+  constexpr uint32_t idesc_qk = idesc_f16_f32(kBlockM, kBlockN, false);
+  constexpr uint32_t idesc_pv = idesc_f16_f32(kBlockM, kHeadDim, true);
+  uint32_t base = 0;                 // K/V loads consumed before the current item
+  uint32_t q_count = 0;
+  uint32_t s_cnt[2] = {0, 0}, p_cnt[2] = {0, 0}, o_cnt[2] = {0, 0};
+  const uint32_t sq[2] = {smem_base + kSmemQ, smem_base + kSmemQ + kTileBytes};
+
+  auto wait = [&](uint32_t bar, uint32_t parity) {
+    return mbar_wait(bar, parity, abort_flag, p.status, kStatusTimeoutMma, p.limit_ns);
+  };
+
+  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+    const ItemShape s = decode_item(item, p);
+    if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
+    ++q_count;
+    tc_fence_after();
+    for (int j = 0; j <= s.n_max; ++j) {
+      if (j < s.n_max) {
+        // ---- S_t = Q_t K_j^T for every tile that still needs key tile j
+        const uint32_t idx = base + 2 * j;
+        const uint32_t ks = idx % kKvSlots;
+        if (!wait(smem_u32(&ctl->kv_full[ks]), (idx / kKvSlots) & 1)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_base + kSmemKV + ks * kTileBytes;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (j >= s.n_t[t]) continue;
+          if (!wait(smem_u32(&ctl->s_empty[t]), (s_cnt[t] & 1) ^ 1)) return false;
+          ++s_cnt[t];
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+            const uint64_t a = smem_desc_sw128(sq[t] + kk * 32, 16, 1024);
+            const uint64_t b = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
+            mma_ss_f16(tmem + col_s(t), a, b, idesc_qk, kk > 0);
+          }
+          tc_commit(smem_u32(&ctl->s_full[t]));
+        }
+        tc_commit(smem_u32(&ctl->kv_empty[ks]));
+        if (j == s.n_max - 1) tc_commit(smem_u32(&ctl->q_empty));
+      }
+      if (j > 0) {
+        // ---- O_t += P_t V_{j-1}
+        const int jj = j - 1;
+        const uint32_t idx = base + 2 * jj + 1;
+        const uint32_t vs = idx % kKvSlots;
+        if (!wait(smem_u32(&ctl->kv_full[vs]), (idx / kKvSlots) & 1)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_base + kSmemKV + vs * kTileBytes;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (jj >= s.n_t[t]) continue;
+          if (jj == 0) {
+            // O_t is overwritten by this item's first PV: the previous item's
+            // epilogue must have read it.
+            if (!wait(smem_u32(&ctl->o_empty[t]), (o_cnt[t] & 1) ^ 1)) return false;
+            ++o_cnt[t];
+          }
+          if (!wait(smem_u32(&ctl->p_full[t]), p_cnt[t] & 1)) return false;
+          ++p_cnt[t];
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBlockN / 16; ++kk) {
+            // P: 16 keys = 8 packed columns per step; V: 16 key rows = 2 KiB.
+            const uint64_t b = smem_desc_sw128(v_addr + kk * 2048, 16, 1024);
+            mma_ts_f16(tmem + col_o(t), tmem + col_p(t) + kk * 8, b, idesc_pv,
+                       (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&ctl->o_done[t]));
+        }
+        tc_commit(smem_u32(&ctl->kv_empty[vs]));
+      }
+    }
+    base += 2 * s.n_max;
+  }
+  return true;
+}
+
+__device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
+                             uint32_t tmem, const CUtensorMap* tm_o, int t, int warp_in_group,
+                             int lane) {
+  volatile int* abort_flag = &ctl->abort;
+  const int row = warp_in_group * 32 + lane;
+  const uint32_t lane_base = static_cast<uint32_t>(warp_in_group * 32) << 16;
+  const uint32_t t_s = tmem + lane_base + col_s(t);
+  const uint32_t t_o = tmem + lane_base + col_o(t);
+  const uint32_t t_p = tmem + lane_base + col_p(t);
+  const uint32_t s_full = smem_u32(&ctl->s_full[t]);
+  const uint32_t s_empty = smem_u32(&ctl->s_empty[t]);
+  const uint32_t p_full = smem_u32(&ctl->p_full[t]);
+  const uint32_t o_done = smem_u32(&ctl->o_done[t]);
+  const uint32_t o_empty = smem_u32(&ctl->o_empty[t]);
+  const uint32_t stage = smem_base + kSmemO + t * kTileBytes;
+  const float c = p.scale_log2;
+  const bool leader = (row == 0);
+  uint32_t s_cnt = 0, od_cnt = 0;
+  bool first_item = true;
+
+  auto wait = [&](uint32_t bar, uint32_t parity) {
+    return mbar_wait(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax, p.limit_ns);
+  };
+
+  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+    const ItemShape s = decode_item(item, p);
+    const int n_t = s.n_t[t];
+    if (n_t == 0) continue;
+    const int q_row = s.q0[t] + row;
+    float m_used = -INFINITY;
+    float l = 0.f;
+
+    for (int j = 0; j < n_t; ++j) {
+      if (!wait(s_full, s_cnt & 1)) return false;
+      ++s_cnt;
+      tc_fence_after();
+      uint32_t sr[128];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tmem_ld32(t_s + 32 * i, sr + 32 * i);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_empty);
+
+      const int kv0 = j * kBlockN;
+      const bool need_mask =
+          (p.causal && kv0 + kBlockN - 1 > s.q0[t]) || (kv0 + kBlockN > p.n_k);
+      if (need_mask) {
+        const int lim_causal = p.causal ? (q_row - kv0) : (kBlockN - 1);
+        const int lim_tail = p.n_k - kv0 - 1;
+        const int lim = lim_causal < lim_tail ? lim_causal : lim_tail;
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i > lim) sr[i] = __float_as_uint(-INFINITY);
+      }
+      if (p.dbg != nullptr && item == static_cast<int>(blockIdx.x) && blockIdx.x == 0 && j == 0) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) p.dbg[(t * 128 + row) * 128 + i] = __uint_as_float(sr[i]);
+      }
+
+      float mx = __uint_as_float(sr[0]);
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
+      const float m_new = fmaxf(m_used, mx);
+      const bool rescale = (m_new - m_used) * c > 8.0f;
+      float alpha = 1.f;
+      if (rescale) {
+        alpha = ex2_approx((m_used - m_new) * c);
+        m_used = m_new;
+        l *= alpha;
+      }
+      const float neg = -m_used * c;
+      uint32_t pk[64];
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), c, neg));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), c, neg));
+        sum0 += p0;
+        sum1 += p1;
+        pk[i] = pack_half2(p0, p1);
+      }
+      l += sum0 + sum1;
+
+      if (j > 0) {
+        // PV(j-1) must be done before P_t is overwritten or O_t is rescaled.
+        if (!wait(o_done, od_cnt & 1)) return false;
+        ++od_cnt;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+          uint32_t orr[64];
+          tmem_ld32(t_o, orr);
+          tmem_ld32(t_o + 32, orr + 32);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 64; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+          tmem_st32(t_o, orr);
+          tmem_st32(t_o + 32, orr + 32);
+        }
+      }
+      tmem_st32(t_p, pk);
+      tmem_st32(t_p + 32, pk + 32);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+
+    // ---- epilogue: O / l -> fp16 -> swizzled staging tile -> TMA store
+    if (!wait(o_done, od_cnt & 1)) return false;
+    ++od_cnt;
+    tc_fence_after();
+    uint32_t orr[64];
+    tmem_ld32(t_o, orr);
+    tmem_ld32(t_o + 32, orr + 32);
+    tc_wait_ld();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(o_empty);
+
+    const float inv = 1.f / l;
+    uint32_t h[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      h[i] = pack_half2(__uint_as_float(orr[2 * i]) * inv, __uint_as_float(orr[2 * i + 1]) * inv);
+
+    if (leader && !first_item) bulk_wait_group_read0();
+    named_bar_sync(1 + t, 128);
+    const uint32_t row_addr = stage + row * 128;
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const uint32_t dst = row_addr + ((ch ^ (row & 7)) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(h[4 * ch]),
+                   "r"(h[4 * ch + 1]), "r"(h[4 * ch + 2]), "r"(h[4 * ch + 3])
+                   : "memory");
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(1 + t, 128);
+    if (leader) {
+      tma_store_3d(tm_o, stage, 0, s.q0[t], s.bh);
+      bulk_commit_group();
+    }
+    first_item = false;
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kNumThreads, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t smem_base = (raw + 1023u) & ~1023u;  // SW128 tiles need 1 KiB alignment
+  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(smem_raw + (smem_base - raw) + kSmemCtl);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&ctl->q_full), 1);
+    mbar_init(smem_u32(&ctl->q_empty), 1);
+    for (int i = 0; i < kKvSlots; ++i) {
+      mbar_init(smem_u32(&ctl->kv_full[i]), 1);
+      mbar_init(smem_u32(&ctl->kv_empty[i]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&ctl->s_full[t]), 1);
+      mbar_init(smem_u32(&ctl->s_empty[t]), 4);
+      mbar_init(smem_u32(&ctl->p_full[t]), 4);
+      mbar_init(smem_u32(&ctl->o_done[t]), 1);
+      mbar_init(smem_u32(&ctl->o_empty[t]), 4);
+    }
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp < 8) {
+    const bool ok = softmax_loop(p, ctl, smem_base, tmem, &tm_o, warp / 4, warp % 4, lane);
+    (void)ok;
+    if (warp % 4 == 0 && lane == 0) bulk_wait_group0();
+  } else if (warp == 8) {
+    if (lane == 0) {
+      uint32_t ld_count = 0, q_count = 0;
+      const bool ok = producer_loop(p, ctl, smem_base, &tm_q, &tm_k, &tm_v, ld_count, q_count);
+      if (!ok) {
+        // Let every copy this thread started land before the block exits.
+        const uint32_t n = ld_count < kKvSlots ? ld_count : kKvSlots;
+        for (uint32_t i = 0; i < n; ++i) {
+          const uint32_t idx = ld_count - 1 - i;
+          mbar_wait(smem_u32(&ctl->kv_full[idx % kKvSlots]), (idx / kKvSlots) & 1, nullptr,
+                    p.status, kStatusTimeoutDrain, p.limit_ns);
+        }
+        if (q_count > 0)
+          mbar_wait(smem_u32(&ctl->q_full), (q_count - 1) & 1, nullptr, p.status,
+                    kStatusTimeoutDrain, p.limit_ns);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    if (lane == 0) {
+      mma_loop(p, ctl, smem_base, tmem);
+      // Every MMA (and the barrier arrivals its commits perform) finishes
+      // before tensor memory and shared memory are released.
+      tc_commit(smem_u32(&ctl->drain));
+      mbar_wait(smem_u32(&ctl->drain), 0, nullptr, p.status, kStatusTimeoutDrain, p.limit_ns);
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+__global__ void selftest_timeout_kernel(unsigned int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Nothing ever arrives on this barrier: the wait must give up by itself.
+    mbar_wait(smem_u32(&bar), 0, &abort_flag, status, kStatusTimeoutSelftest, limit_ns);
+  }
+}
+
+__device__ unsigned int g_status_word;
+
+}  // namespace fa
+
+// ====================================================================== host
+namespace {
+
+thread_local char g_last_error[512] = "";
+unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+  bool ready = false;
+  int sms = 0;
+  unsigned int* status = nullptr;
+};
+DeviceState g_dev[kMaxDevices];
+EncodeTiledFn g_encode = nullptr;
+std::mutex g_mutex;
+
+int ensure_device(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(FA_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& d = g_dev[dev];
+  if (!d.ready) {
+    if (g_encode == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess)
+        return set_error(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s",
+                         cudaGetErrorString(e));
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return set_error(FA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this kernel needs sm_100", dev,
+                       major, minor);
+    cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "%s", cudaGetErrorString(e));
+    e = cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(fa::kSmemBytes));
+    if (e != cudaSuccess)
+      return set_error(FA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    void* sym = nullptr;
+    e = cudaGetSymbolAddress(&sym, fa::g_status_word);
+    if (e != cudaSuccess)
+      return set_error(FA_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    d.status = static_cast<unsigned int*>(sym);
+    d.ready = true;
+  }
+  *out = &d;
+  return FA_OK;
+}
+
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t slices) {
+  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(slices)};
+  const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(rows) * 128};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims,
+                        strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FA_OK;
+}
+
+int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int64_t n_q,
+           int64_t n_k, int causal, float scale, cudaStream_t stream, float* dbg) {
+  if (bh < 0 || n_q < 0 || n_k < 0) return set_error(FA_ERR_INVALID, "negative size");
+  if (bh == 0 || n_q == 0) return FA_OK;
+  if (n_k == 0) return set_error(FA_ERR_INVALID, "key length must be positive when queries exist");
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
+    return set_error(FA_ERR_INVALID, "null pointer");
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o);
+  if (mis & 15) return set_error(FA_ERR_INVALID, "q, k, v and o must be 16-byte aligned");
+  if (n_q > (1ll << 30) || n_k > (1ll << 30) || bh > (1ll << 30))
+    return set_error(FA_ERR_INVALID, "size too large");
+  if (!(scale > 0.f) || !std::isfinite(scale)) return set_error(FA_ERR_INVALID, "scale must be positive and finite");
+  const int64_t n_qpairs = ((n_q + 127) / 128 + 1) / 2;
+  if (bh * n_qpairs > 0x7fffffffll) return set_error(FA_ERR_INVALID, "too many work items");
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  DeviceState* d = nullptr;
+  int rc = ensure_device(dev, &d);
+  if (rc != FA_OK) return rc;
+
+  CUtensorMap tq, tk, tv, to;
+  if ((rc = make_map(&tq, q, n_q, bh)) != FA_OK) return rc;
+  if ((rc = make_map(&tk, k, n_k, bh)) != FA_OK) return rc;
+  if ((rc = make_map(&tv, v, n_k, bh)) != FA_OK) return rc;
+  if ((rc = make_map(&to, o, n_q, bh)) != FA_OK) return rc;
+
+  fa::FwdParams p;
+  p.n_q = static_cast<int>(n_q);
+  p.n_k = static_cast<int>(n_k);
+  p.bh = static_cast<int>(bh);
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.n_qpairs = static_cast<int>(n_qpairs);
+  p.n_items = static_cast<int>(bh * n_qpairs);
+  p.status = d->status;
+  p.limit_ns = g_wait_limit_ns;
+  p.dbg = dbg;
+
+  const int grid = p.n_items < d->sms ? p.n_items : d->sms;
+  fa::fa_fwd_kernel<<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_fwd_sm100(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                 int64_t heads, int64_t seq_len, int causal, float scale, void* cuda_stream) {
+  if (batch < 0 || heads < 0) return set_error(FA_ERR_INVALID, "negative size");
+  return launch(q, k, v, o, batch * heads, seq_len, seq_len, causal, scale,
+                static_cast<cudaStream_t>(cuda_stream), nullptr);
+}
+
+int fa_fwd_sm100_varlen(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                        int64_t heads, int64_t q_len, int64_t kv_len, int causal, float scale,
+                        void* cuda_stream) {
+  if (batch < 0 || heads < 0) return set_error(FA_ERR_INVALID, "negative size");
+  return launch(q, k, v, o, batch * heads, q_len, kv_len, causal, scale,
+                static_cast<cudaStream_t>(cuda_stream), nullptr);
+}
+
+int fa_fwd_sm100_debug(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                       int64_t heads, int64_t seq_len, int causal, float scale, void* cuda_stream,
+                       float* score_dump) {
+  return launch(q, k, v, o, batch * heads, seq_len, seq_len, causal, scale,
+                static_cast<cudaStream_t>(cuda_stream), score_dump);
+}
+
+const char* fa_last_error(void) { return g_last_error; }
+
+int fa_read_status(void* cuda_stream, unsigned int* status_out, int clear) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  DeviceState* d = nullptr;
+  int rc = ensure_device(dev, &d);
+  if (rc != FA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+  unsigned int v = 0;
+  e = cudaMemcpyAsync(&v, d->status, sizeof(v), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+  if (clear) {
+    e = cudaMemsetAsync(d->status, 0, sizeof(unsigned int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "status clear: %s", cudaGetErrorString(e));
+  }
+  if (status_out) *status_out = v;
+  return FA_OK;
+}
+
+void fa_set_wait_limit_ns(unsigned long long limit_ns) {
+  g_wait_limit_ns = limit_ns == 0 ? 2000000000ull : limit_ns;
+}
+
+int fa_selftest_wait_timeout(unsigned long long limit_ns, void* cuda_stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  DeviceState* d = nullptr;
+  int rc = ensure_device(dev, &d);
+  if (rc != FA_OK) return rc;
+  fa::selftest_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(cuda_stream)>>>(d->status,
+                                                                                  limit_ns);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return FA_OK;
+}
+
+int fa_smem_bytes(void) { return static_cast<int>(fa::kSmemBytes); }
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+/*
+ * C ABI of the B200 (sm_100a) FlashAttention forward library
+ * (libfa_sm100.so). Plain pointers, sizes and a CUDA stream handle; no
+ * PyTorch types. Every function returns FA_OK (0) or a negative FA_ERR_*
+ * code; fa_last_error() then holds a message for the calling thread.
+ *
+ * Layout of every tensor: contiguous [batch, heads, rows, 64] fp16, so one
+ * (batch, head) slice is rows x 128 bytes. Pointers must be device pointers
+ * on the current CUDA device and 16-byte aligned. Work is enqueued on
+ * `cuda_stream` (NULL = legacy default stream); nothing synchronises.
+ */
+#ifndef FA_SM100_H_
+#define FA_SM100_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA_OK 0
+#define FA_ERR_INVALID (-1)     /* bad sizes, pointers or alignment */
+#define FA_ERR_CUDA (-2)        /* CUDA runtime / driver call failed */
+#define FA_ERR_UNSUPPORTED (-3) /* device is not sm_100 */
+
+/*
+ * Attention forward, head dimension 64, equal query and key lengths.
+ * O = softmax(Q K^T * scale [+ causal mask]) V with fp32 accumulation and fp16
+ * output. `causal` masks key index > query index (top-left aligned).
+ *
+ * Replaces the launch path of the reference's production kernel:
+ *   tensorcore_attention_forward_production_impl
+ *     (csrc/tensorcore_attention.cu:2969-3123), which launches
+ *   tensorcore_attention_forward_kernel_d64_production<kCausal>
+ *     (csrc/tensorcore_attention.cu:2019-2727) with scale 1/sqrt(64)
+ *     (csrc/tensorcore_attention.cu:3040-3046).
+ * Unlike the reference launcher, seq_len need not be a multiple of 128 and
+ * batch * heads is not limited to 65535 (persistent grid); the torch binding
+ * keeps the reference's checks for drop-in behaviour.
+ * batch * heads * seq_len == 0 is a no-op (reference :3003-3009).
+ */
+int fa_fwd_sm100(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                 int64_t heads, int64_t seq_len, int causal, float scale, void* cuda_stream);
+
+/*
+ * Same, with independent query and key lengths (k and v have kv_len rows,
+ * q and o have q_len rows). The causal mask stays top-left aligned, as in
+ * the reference oracle flash_attention/reference.py:49-56 (triu(1) on an
+ * [q_len, kv_len] matrix).
+ */
+int fa_fwd_sm100_varlen(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                        int64_t heads, int64_t q_len, int64_t kv_len, int causal, float scale,
+                        void* cuda_stream);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* fa_last_error(void);
+
+/*
+ * Reads (and with clear != 0 resets) the device status word of the current
+ * device, synchronising `cuda_stream`. Nonzero bits mean a bounded wait inside
+ * a kernel ran out of time and that launch's output is invalid:
+ *   1 producer, 2 MMA issuer, 4 softmax, 8 drain, 16 self-test.
+ * No counterpart in the reference (its kernel has no waits that can fail).
+ */
+int fa_read_status(void* cuda_stream, unsigned int* status_out, int clear);
+
+/* Time limit for every in-kernel wait (default 2 s; 0 restores it). */
+void fa_set_wait_limit_ns(unsigned long long limit_ns);
+
+/*
+ * Launches a one-warp kernel that waits on a barrier nothing arrives on,
+ * with the given limit; afterwards fa_read_status must report bit 16.
+ * Exercises the timeout path without faulting or hanging the GPU.
+ */
+int fa_selftest_wait_timeout(unsigned long long limit_ns, void* cuda_stream);
+
+/* Dynamic shared memory one block of the forward kernel uses (bytes). */
+int fa_smem_bytes(void);
+
+/*
+ * Test hook: as fa_fwd_sm100, and additionally writes the first work item's
+ * first masked score tile (256 x 128 fp32, raw Q K^T before scaling) to
+ * score_dump. Used only by the tests to localise layout errors.
+ */
+int fa_fwd_sm100_debug(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                       int64_t heads, int64_t seq_len, int causal, float scale, void* cuda_stream,
+                       float* score_dump);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_SM100_H_ */
