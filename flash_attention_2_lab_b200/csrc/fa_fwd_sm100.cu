@@ -7,7 +7,7 @@
 //
 //   warp 8      TMA producer: Q tiles of the current work item, then K_j/V_j
 //               tiles through a ring of swizzled shared-memory slots.
-//   warp 9      MMA issuer (one thread): S_t = Q_t K_j^T (SS form) and
+//   warp 9      MMA issuer (one elected lane): S_t = Q_t K_j^T (SS form) and
 //               O_t += P_t V_j (P read straight from tensor memory, TS form).
 //               It also owns the tensor-memory allocation.
 //   warps 0-3   softmax for query tile 0 of the work item, one thread per row.
@@ -45,7 +45,7 @@
 #include <mutex>
 
 #include "sm100_ptx.cuh"
-#include "../../include/fa_sm100.h"
+#include "fa_sm100.h"
 
 namespace fa {
 using namespace ptx;
@@ -128,52 +128,70 @@ __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
 }
 
 // ------------------------------------------------------------------ roles
+// Runs on the whole producer warp; one elected lane issues the copies.
 __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                               const CUtensorMap* tm_q, const CUtensorMap* tm_k,
                               const CUtensorMap* tm_v, uint32_t& ld_count, uint32_t& q_count) {
   volatile int* abort_flag = &ctl->abort;
   const uint32_t q_full = smem_u32(&ctl->q_full), q_empty = smem_u32(&ctl->q_empty);
+  uint32_t slot = 0, phase = 0;
   for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
     const ItemShape s = decode_item(item, p);
-    if (!mbar_wait(q_empty, (q_count & 1) ^ 1, abort_flag, p.status, kStatusTimeoutProducer,
-                   p.limit_ns))
+    if (!mbar_wait_warp(q_empty, (q_count & 1) ^ 1, abort_flag, p.status,
+                        kStatusTimeoutProducer, p.limit_ns))
       return false;
     const uint32_t nq = (s.n_t[1] > 0) ? 2 : 1;
-    mbar_arrive_expect_tx(q_full, nq * kTileBytes);
-    tma_load_3d(smem_base + kSmemQ, tm_q, q_full, 0, s.q0[0], s.bh);
-    if (nq == 2) tma_load_3d(smem_base + kSmemQ + kTileBytes, tm_q, q_full, 0, s.q0[1], s.bh);
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, nq * kTileBytes);
+      tma_load_3d(smem_base + kSmemQ, tm_q, q_full, 0, s.q0[0], s.bh);
+      if (nq == 2) tma_load_3d(smem_base + kSmemQ + kTileBytes, tm_q, q_full, 0, s.q0[1], s.bh);
+    }
+    __syncwarp();
     ++q_count;
     for (int j = 0; j < s.n_max; ++j) {
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
-        const uint32_t slot = ld_count % kKvSlots;
-        const uint32_t phase = (ld_count / kKvSlots) & 1;
-        if (!mbar_wait(smem_u32(&ctl->kv_empty[slot]), phase ^ 1, abort_flag, p.status,
-                       kStatusTimeoutProducer, p.limit_ns))
+        if (!mbar_wait_warp(smem_u32(&ctl->kv_empty[slot]), phase ^ 1, abort_flag, p.status,
+                            kStatusTimeoutProducer, p.limit_ns))
           return false;
-        const uint32_t full = smem_u32(&ctl->kv_full[slot]);
-        mbar_arrive_expect_tx(full, kTileBytes);
-        tma_load_3d(smem_base + kSmemKV + slot * kTileBytes, which ? tm_v : tm_k, full, 0,
-                    j * kBlockN, s.bh);
+        if (elect_one()) {
+          const uint32_t full = smem_u32(&ctl->kv_full[slot]);
+          mbar_arrive_expect_tx(full, kTileBytes);
+          tma_load_3d(smem_base + kSmemKV + slot * kTileBytes, which ? tm_v : tm_k, full, 0,
+                      j * kBlockN, s.bh);
+        }
+        __syncwarp();
         ++ld_count;
+        if (++slot == kKvSlots) {
+          slot = 0;
+          phase ^= 1;
+        }
       }
     }
   }
   return true;
 }
 
+// Runs on the whole MMA warp: waits and bookkeeping are warp-uniform (so the
+// descriptors live in uniform registers) and one elected lane issues the
+// tcgen05 instructions.  Per key tile j the issue order is
+//   S_0(j), S_1(j), O_0 += P_0(j-1) V_{j-1}, O_1 += P_1(j-1) V_{j-1}.
 __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                          uint32_t tmem) {
   volatile int* abort_flag = &ctl->abort;
   constexpr uint32_t idesc_qk = idesc_f16_f32(kBlockM, kBlockN, false);
   constexpr uint32_t idesc_pv = idesc_f16_f32(kBlockM, kHeadDim, true);
-  uint32_t base = 0;                 // K/V loads consumed before the current item
+  uint32_t slot = 0, phase = 0;  // ring position of the next K tile
   uint32_t q_count = 0;
   uint32_t s_cnt[2] = {0, 0}, p_cnt[2] = {0, 0}, o_cnt[2] = {0, 0};
-  const uint32_t sq[2] = {smem_base + kSmemQ, smem_base + kSmemQ + kTileBytes};
+  // Descriptor bases; the start-address field (bits 0-13, 16-byte units) is
+  // advanced by plain addition: every operand lies below 256 KiB.
+  const uint64_t dq0 = smem_desc_sw128(smem_base + kSmemQ, 16, 1024);
+  const uint64_t dkv = smem_desc_sw128(smem_base + kSmemKV, 16, 1024);
+  constexpr uint64_t kTileDesc = kTileBytes >> 4;
 
   auto wait = [&](uint32_t bar, uint32_t parity) {
-    return mbar_wait(bar, parity, abort_flag, p.status, kStatusTimeoutMma, p.limit_ns);
+    return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutMma, p.limit_ns);
   };
 
   for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
@@ -181,39 +199,49 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
     if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
     ++q_count;
     tc_fence_after();
+    uint32_t v_slot = 0, v_phase = 0;  // ring position of V_{j-1}
     for (int j = 0; j <= s.n_max; ++j) {
+      uint32_t next_v_slot = 0, next_v_phase = 0;
       if (j < s.n_max) {
         // ---- S_t = Q_t K_j^T for every tile that still needs key tile j
-        const uint32_t idx = base + 2 * j;
-        const uint32_t ks = idx % kKvSlots;
-        if (!wait(smem_u32(&ctl->kv_full[ks]), (idx / kKvSlots) & 1)) return false;
+        const uint32_t ks = slot, kph = phase;
+        next_v_slot = ks + 1 == kKvSlots ? 0 : ks + 1;
+        next_v_phase = ks + 1 == kKvSlots ? kph ^ 1 : kph;
+        slot += 2;  // past K_j and V_j
+        if (slot >= kKvSlots) {
+          slot -= kKvSlots;
+          phase ^= 1;
+        }
+        if (!wait(smem_u32(&ctl->kv_full[ks]), kph)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_base + kSmemKV + ks * kTileBytes;
+        const uint64_t dk = dkv + ks * kTileDesc;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j >= s.n_t[t]) continue;
           if (!wait(smem_u32(&ctl->s_empty[t]), (s_cnt[t] & 1) ^ 1)) return false;
           ++s_cnt[t];
           tc_fence_after();
+          if (elect_one()) {
+            const uint64_t dq = dq0 + t * kTileDesc;
 #pragma unroll
-          for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-            const uint64_t a = smem_desc_sw128(sq[t] + kk * 32, 16, 1024);
-            const uint64_t b = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-            mma_ss_f16(tmem + col_s(t), a, b, idesc_qk, kk > 0);
+            for (int kk = 0; kk < kHeadDim / 16; ++kk)  // 16 dims = 32 bytes per step
+              mma_ss_f16(tmem + col_s(t), dq + 2 * kk, dk + 2 * kk, idesc_qk, kk > 0);
+            tc_commit(smem_u32(&ctl->s_full[t]));
           }
-          tc_commit(smem_u32(&ctl->s_full[t]));
+          __syncwarp();
         }
-        tc_commit(smem_u32(&ctl->kv_empty[ks]));
-        if (j == s.n_max - 1) tc_commit(smem_u32(&ctl->q_empty));
+        if (elect_one()) {
+          tc_commit(smem_u32(&ctl->kv_empty[ks]));
+          if (j == s.n_max - 1) tc_commit(smem_u32(&ctl->q_empty));
+        }
+        __syncwarp();
       }
       if (j > 0) {
         // ---- O_t += P_t V_{j-1}
         const int jj = j - 1;
-        const uint32_t idx = base + 2 * jj + 1;
-        const uint32_t vs = idx % kKvSlots;
-        if (!wait(smem_u32(&ctl->kv_full[vs]), (idx / kKvSlots) & 1)) return false;
+        if (!wait(smem_u32(&ctl->kv_full[v_slot]), v_phase)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_base + kSmemKV + vs * kTileBytes;
+        const uint64_t dv = dkv + v_slot * kTileDesc;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (jj >= s.n_t[t]) continue;
@@ -226,19 +254,23 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
           if (!wait(smem_u32(&ctl->p_full[t]), p_cnt[t] & 1)) return false;
           ++p_cnt[t];
           tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < kBlockN / 16; ++kk) {
-            // P: 16 keys = 8 packed columns per step; V: 16 key rows = 2 KiB.
-            const uint64_t b = smem_desc_sw128(v_addr + kk * 2048, 16, 1024);
-            mma_ts_f16(tmem + col_o(t), tmem + col_p(t) + kk * 8, b, idesc_pv,
-                       (jj > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kBlockN / 16; ++kk) {
+              // P: 16 keys = 8 packed columns per step; V: 16 key rows = 2 KiB.
+              mma_ts_f16(tmem + col_o(t), tmem + col_p(t) + kk * 8, dv + 128 * kk, idesc_pv,
+                         (jj > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit(smem_u32(&ctl->o_done[t]));
           }
-          tc_commit(smem_u32(&ctl->o_done[t]));
+          __syncwarp();
         }
-        tc_commit(smem_u32(&ctl->kv_empty[vs]));
+        if (elect_one()) tc_commit(smem_u32(&ctl->kv_empty[v_slot]));
+        __syncwarp();
       }
+      v_slot = next_v_slot;
+      v_phase = next_v_phase;
     }
-    base += 2 * s.n_max;
   }
   return true;
 }
@@ -303,10 +335,19 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
         for (int i = 0; i < 128; ++i) p.dbg[(t * 128 + row) * 128 + i] = __uint_as_float(sr[i]);
       }
 
-      float mx = __uint_as_float(sr[0]);
+      // Row max: eight independent chains of three-input maxima.
+      float mx[8];
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-      const float m_new = fmaxf(m_used, mx);
+      for (int a = 0; a < 8; ++a) {
+        const uint32_t* g = sr + 16 * a;
+        float acc = max3f(__uint_as_float(g[0]), __uint_as_float(g[1]), __uint_as_float(g[2]));
+#pragma unroll
+        for (int e = 3; e + 1 < 16; e += 2)
+          acc = max3f(acc, __uint_as_float(g[e]), __uint_as_float(g[e + 1]));
+        mx[a] = fmaxf(acc, __uint_as_float(g[15]));
+      }
+      const float m_new = max3f(max3f(mx[0], mx[1], mx[2]), max3f(mx[3], mx[4], mx[5]),
+                                max3f(mx[6], mx[7], m_used));
       const bool rescale = (m_new - m_used) * c > 8.0f;
       float alpha = 1.f;
       if (rescale) {
@@ -315,17 +356,23 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
         l *= alpha;
       }
       const float neg = -m_used * c;
+
+      // p = 2^(s*c - m*c): packed FMA for the exponent, MUFU ex2, packed sums
+      // in eight independent chains, fp16 pairs kept in registers until P_t is
+      // free again.
       uint32_t pk[64];
-      float sum0 = 0.f, sum1 = 0.f;
+      float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), c, neg));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), c, neg));
-        sum0 += p0;
-        sum1 += p1;
+        float x0, x1;
+        ffma2(x0, x1, __uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]), c, c, neg, neg);
+        const float p0 = ex2_approx(x0);
+        const float p1 = ex2_approx(x1);
+        const int a = (i & 3) * 2;
+        fadd2(sum[a], sum[a + 1], sum[a], sum[a + 1], p0, p1);
         pk[i] = pack_half2(p0, p1);
       }
-      l += sum0 + sum1;
+      l += ((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7]));
 
       if (j > 0) {
         // PV(j-1) must be done before P_t is overwritten or O_t is rescaled.
@@ -338,7 +385,13 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
           tmem_ld32(t_o + 32, orr + 32);
           tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 64; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+          for (int i = 0; i < 32; ++i) {
+            float a0, a1;
+            fmul2(a0, a1, __uint_as_float(orr[2 * i]), __uint_as_float(orr[2 * i + 1]), alpha,
+                  alpha);
+            orr[2 * i] = __float_as_uint(a0);
+            orr[2 * i + 1] = __float_as_uint(a1);
+          }
           tmem_st32(t_o, orr);
           tmem_st32(t_o + 32, orr + 32);
         }
@@ -436,32 +489,36 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
 
   if (warp < 8) {
+    // Softmax warpgroups take the registers the producer/MMA warpgroup gives
+    // up: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     const bool ok = softmax_loop(p, ctl, smem_base, tmem, &tm_o, warp / 4, warp % 4, lane);
     (void)ok;
     if (warp % 4 == 0 && lane == 0) bulk_wait_group0();
-  } else if (warp == 8) {
-    if (lane == 0) {
-      uint32_t ld_count = 0, q_count = 0;
-      const bool ok = producer_loop(p, ctl, smem_base, &tm_q, &tm_k, &tm_v, ld_count, q_count);
-      if (!ok) {
-        // Let every copy this thread started land before the block exits.
-        const uint32_t n = ld_count < kKvSlots ? ld_count : kKvSlots;
-        for (uint32_t i = 0; i < n; ++i) {
-          const uint32_t idx = ld_count - 1 - i;
-          mbar_wait(smem_u32(&ctl->kv_full[idx % kKvSlots]), (idx / kKvSlots) & 1, nullptr,
-                    p.status, kStatusTimeoutDrain, p.limit_ns);
-        }
-        if (q_count > 0)
-          mbar_wait(smem_u32(&ctl->q_full), (q_count - 1) & 1, nullptr, p.status,
-                    kStatusTimeoutDrain, p.limit_ns);
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+  }
+  if (warp == 8) {
+    uint32_t ld_count = 0, q_count = 0;
+    const bool ok = producer_loop(p, ctl, smem_base, &tm_q, &tm_k, &tm_v, ld_count, q_count);
+    if (!ok && lane == 0) {
+      // Let every copy this warp started land before the block exits.
+      const uint32_t n = ld_count < kKvSlots ? ld_count : kKvSlots;
+      for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t idx = ld_count - 1 - i;
+        mbar_wait(smem_u32(&ctl->kv_full[idx % kKvSlots]), (idx / kKvSlots) & 1, nullptr,
+                  p.status, kStatusTimeoutDrain, p.limit_ns);
       }
+      if (q_count > 0)
+        mbar_wait(smem_u32(&ctl->q_full), (q_count - 1) & 1, nullptr, p.status,
+                  kStatusTimeoutDrain, p.limit_ns);
     }
     __syncwarp();
   } else if (warp == 9) {
+    mma_loop(p, ctl, smem_base, tmem);
+    // Every MMA (and the barrier arrivals its commits perform) finishes
+    // before tensor memory and shared memory are released.
     if (lane == 0) {
-      mma_loop(p, ctl, smem_base, tmem);
-      // Every MMA (and the barrier arrivals its commits perform) finishes
-      // before tensor memory and shared memory are released.
       tc_commit(smem_u32(&ctl->drain));
       mbar_wait(smem_u32(&ctl->drain), 0, nullptr, p.status, kStatusTimeoutDrain, p.limit_ns);
     }
