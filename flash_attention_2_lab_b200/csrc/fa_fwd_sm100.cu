@@ -47,8 +47,34 @@
 #include "sm100_ptx.cuh"
 #include "fa_sm100.h"
 
+#ifndef FA_TRACE
+#define FA_TRACE 0
+#endif
+#ifndef FA_POLY_PAIRS
+#define FA_POLY_PAIRS 0  // of every 8 exponent pairs, this many use the FMA-pipe polynomial
+#endif
+#ifndef FA_EARLY_PASS
+#define FA_EARLY_PASS 16  // exponent pairs still to do when the MUFU turn is handed over
+#endif
+
 namespace fa {
 using namespace ptx;
+
+// Development aid, compiled in only with -DFA_TRACE=1: SM clock stamps of the
+// first work item of block 0, written through the debug pointer as
+// trace[role][iteration][event] (role 0/1 softmax tile, 2 MMA issuer).
+#if FA_TRACE
+#define TRACE(role, it, ev)                                                            \
+  do {                                                                                 \
+    if (p.dbg != nullptr && blockIdx.x == 0 && trace_on && (it) < 64)                   \
+      reinterpret_cast<unsigned long long*>(p.dbg)[((role) * 64 + (it)) * 8 + (ev)] =  \
+          clock64();                                                                   \
+  } while (0)
+#else
+#define TRACE(role, it, ev) \
+  do {                      \
+  } while (0)
+#endif
 
 constexpr int kHeadDim = 64;
 constexpr int kBlockM = 128;   // query rows per tile
@@ -80,6 +106,7 @@ struct SharedCtl {
   uint64_t q_full, q_empty;
   uint64_t kv_full[kKvSlots], kv_empty[kKvSlots];
   uint64_t s_full[2], s_empty[2], p_full[2], o_done[2], o_empty[2];
+  uint64_t exp_turn[2];  // alternates the two softmax warpgroups' exponential phases
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -200,7 +227,10 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
     ++q_count;
     tc_fence_after();
     uint32_t v_slot = 0, v_phase = 0;  // ring position of V_{j-1}
+    const bool trace_on = item == static_cast<int>(blockIdx.x) && threadIdx.x % 32 == 0;
+    (void)trace_on;
     for (int j = 0; j <= s.n_max; ++j) {
+      TRACE(2, j, 0);
       uint32_t next_v_slot = 0, next_v_phase = 0;
       if (j < s.n_max) {
         // ---- S_t = Q_t K_j^T for every tile that still needs key tile j
@@ -213,6 +243,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
           phase ^= 1;
         }
         if (!wait(smem_u32(&ctl->kv_full[ks]), kph)) return false;
+        TRACE(2, j, 1);
         tc_fence_after();
         const uint64_t dk = dkv + ks * kTileDesc;
 #pragma unroll
@@ -220,6 +251,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
           if (j >= s.n_t[t]) continue;
           if (!wait(smem_u32(&ctl->s_empty[t]), (s_cnt[t] & 1) ^ 1)) return false;
           ++s_cnt[t];
+          if (t == 0) TRACE(2, j, 2);
           tc_fence_after();
           if (elect_one()) {
             const uint64_t dq = dq0 + t * kTileDesc;
@@ -229,6 +261,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
             tc_commit(smem_u32(&ctl->s_full[t]));
           }
           __syncwarp();
+          TRACE(2, j, 3 + t);
         }
         if (elect_one()) {
           tc_commit(smem_u32(&ctl->kv_empty[ks]));
@@ -240,6 +273,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
         // ---- O_t += P_t V_{j-1}
         const int jj = j - 1;
         if (!wait(smem_u32(&ctl->kv_full[v_slot]), v_phase)) return false;
+        TRACE(2, j, 5);
         tc_fence_after();
         const uint64_t dv = dkv + v_slot * kTileDesc;
 #pragma unroll
@@ -253,6 +287,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
           }
           if (!wait(smem_u32(&ctl->p_full[t]), p_cnt[t] & 1)) return false;
           ++p_cnt[t];
+          if (t == 0) TRACE(2, j, 6);
           tc_fence_after();
           if (elect_one()) {
 #pragma unroll
@@ -264,6 +299,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
             tc_commit(smem_u32(&ctl->o_done[t]));
           }
           __syncwarp();
+          if (t == 0) TRACE(2, j, 7);
         }
         if (elect_one()) tc_commit(smem_u32(&ctl->kv_empty[v_slot]));
         __syncwarp();
@@ -296,25 +332,52 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   bool first_item = true;
 
   auto wait = [&](uint32_t bar, uint32_t parity) {
-    return mbar_wait(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax, p.limit_ns);
+    return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax,
+                          p.limit_ns);
+  };
+
+  // The exponentials of both tiles share the SM's MUFU units (16 ex2/clk).
+  // The two warpgroups take turns (tile 0, tile 1, tile 0, ...), so one's
+  // exponentials overlap the other's P store, S load and row max.  Both run
+  // n_max rounds per work item; a tile with fewer key tiles (or none) passes
+  // its extra turns without work.
+  const uint32_t turn_mine = smem_u32(&ctl->exp_turn[t]);
+  const uint32_t turn_other = smem_u32(&ctl->exp_turn[t ^ 1]);
+  uint32_t turn_cnt = 0;
+  auto take_turn = [&]() { return wait(turn_mine, (turn_cnt & 1) ^ (t == 0 ? 1u : 0u)); };
+  auto pass_turn = [&]() {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(turn_other);
+    ++turn_cnt;
   };
 
   for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
     const ItemShape s = decode_item(item, p);
     const int n_t = s.n_t[t];
-    if (n_t == 0) continue;
+    if (n_t == 0) {
+      for (int j = 0; j < s.n_max; ++j) {
+        if (!take_turn()) return false;
+        pass_turn();
+      }
+      continue;
+    }
     const int q_row = s.q0[t] + row;
     float m_used = -INFINITY;
     float l = 0.f;
 
     for (int j = 0; j < n_t; ++j) {
+      const bool trace_on = item == static_cast<int>(blockIdx.x) && row == 0;
+      (void)trace_on;
+      TRACE(t, j, 0);
       if (!wait(s_full, s_cnt & 1)) return false;
+      TRACE(t, j, 1);
       ++s_cnt;
       tc_fence_after();
       uint32_t sr[128];
 #pragma unroll
       for (int i = 0; i < 4; ++i) tmem_ld32(t_s + 32 * i, sr + 32 * i);
       tc_wait_ld();
+      TRACE(t, j, 2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty);
@@ -330,7 +393,8 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
         for (int i = 0; i < 128; ++i)
           if (i > lim) sr[i] = __float_as_uint(-INFINITY);
       }
-      if (p.dbg != nullptr && item == static_cast<int>(blockIdx.x) && blockIdx.x == 0 && j == 0) {
+      if (!FA_TRACE && p.dbg != nullptr && item == static_cast<int>(blockIdx.x) &&
+          blockIdx.x == 0 && j == 0) {
 #pragma unroll
         for (int i = 0; i < 128; ++i) p.dbg[(t * 128 + row) * 128 + i] = __uint_as_float(sr[i]);
       }
@@ -348,6 +412,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       }
       const float m_new = max3f(max3f(mx[0], mx[1], mx[2]), max3f(mx[3], mx[4], mx[5]),
                                 max3f(mx[6], mx[7], m_used));
+      TRACE(t, j, 3);
       const bool rescale = (m_new - m_used) * c > 8.0f;
       float alpha = 1.f;
       if (rescale) {
@@ -356,6 +421,8 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
         l *= alpha;
       }
       const float neg = -m_used * c;
+      if (!take_turn()) return false;
+      TRACE(t, j, 7);
 
       // p = 2^(s*c - m*c): packed FMA for the exponent, MUFU ex2, packed sums
       // in eight independent chains, fp16 pairs kept in registers until P_t is
@@ -364,20 +431,29 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
+        if (i == 64 - FA_EARLY_PASS) pass_turn();
         float x0, x1;
         ffma2(x0, x1, __uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]), c, c, neg, neg);
-        const float p0 = ex2_approx(x0);
-        const float p1 = ex2_approx(x1);
+        float p0, p1;
+        if ((i & 7) < FA_POLY_PAIRS) {
+          exp2_poly2(p0, p1, x0, x1);
+        } else {
+          p0 = ex2_approx(x0);
+          p1 = ex2_approx(x1);
+        }
         const int a = (i & 3) * 2;
         fadd2(sum[a], sum[a + 1], sum[a], sum[a + 1], p0, p1);
         pk[i] = pack_half2(p0, p1);
       }
+      if (FA_EARLY_PASS == 0) pass_turn();
       l += ((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7]));
+      TRACE(t, j, 4);
 
       if (j > 0) {
         // PV(j-1) must be done before P_t is overwritten or O_t is rescaled.
         if (!wait(o_done, od_cnt & 1)) return false;
         ++od_cnt;
+        TRACE(t, j, 5);
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
           uint32_t orr[64];
@@ -402,6 +478,12 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      TRACE(t, j, 6);
+    }
+
+    for (int j = n_t; j < s.n_max; ++j) {
+      if (!take_turn()) return false;
+      pass_turn();
     }
 
     // ---- epilogue: O / l -> fp16 -> swizzled staging tile -> TMA store
@@ -468,6 +550,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&ctl->p_full[t]), 4);
       mbar_init(smem_u32(&ctl->o_done[t]), 1);
       mbar_init(smem_u32(&ctl->o_empty[t]), 4);
+      mbar_init(smem_u32(&ctl->exp_turn[t]), 4);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;

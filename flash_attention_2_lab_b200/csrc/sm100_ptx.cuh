@@ -60,28 +60,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on the phase with the given parity.  `abort_flag` (shared
-// memory) lets one role that has given up release every other role quickly.
-// On timeout `status` gets `code` OR-ed in and the function returns false.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          volatile int* abort_flag,
-                                          unsigned int* status, unsigned int code,
-                                          uint64_t limit_ns) {
-#pragma unroll 1
-  for (int i = 0; i < 256; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-  }
+// Bounded wait on the phase with the given parity (one thread).  `abort_flag`
+// (shared memory, may be null) lets one role that has given up release every
+// other role quickly.  On timeout `status` gets `code` OR-ed in and the
+// function returns false.
+__device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
+                                            volatile int* abort_flag, unsigned int* status,
+                                            unsigned int code, uint64_t limit_ns) {
   const uint64_t t0 = global_timer_ns();
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
+    if (abort_flag != nullptr && *abort_flag) return false;
     if (global_timer_ns() - t0 > limit_ns) {
       if (status) atomicOr(status, code);
-      *abort_flag = 1;
+      if (abort_flag != nullptr) *abort_flag = 1;
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          volatile int* abort_flag, unsigned int* status,
+                                          unsigned int code, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, status, code, limit_ns);
 }
 
 // One lane of the (converged) warp returns true.
@@ -95,11 +98,14 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
-// Warp-wide bounded wait: every lane polls, the warp agrees on the outcome.
+// Warp-wide bounded wait.  Fast path: one try_wait by every lane, agreed by a
+// vote (about 15 cycles when the phase is already complete); otherwise each
+// lane polls in the out-of-line slow path and the warp agrees on the outcome.
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity,
                                                volatile int* abort_flag, unsigned int* status,
                                                unsigned int code, uint64_t limit_ns) {
-  const bool ok = mbar_wait(bar, parity, abort_flag, status, code, limit_ns);
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const bool ok = mbar_wait_slow(bar, parity, abort_flag, status, code, limit_ns);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -294,6 +300,42 @@ __device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, 
       "mul.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ void fsub2(float& d0, float& d1, float a0, float a1, float b0,
+                                      float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "sub.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^x for a pair of floats on the FMA pipe instead of the MUFU.
+// Cody-Waite style reduction x = j + f with j = rint(x), f in [-1/2, 1/2]
+// (rint by adding and subtracting 1.5 * 2^23), 2^f by a degree-3 polynomial
+// whose coefficients were fitted for minimal relative error on [-1/2, 1/2]
+// (a linear program over 4001 points; max relative error 7.5e-5, below half
+// an fp16 ulp), and 2^j applied by adding j to the exponent field.  x is
+// clamped to >= -125 so the result stays a normal float; a masked score
+// (-inf) therefore gives 2^-125 instead of 0, which rounds to 0 in fp16 and
+// adds nothing measurable to the fp32 row sum.
+__device__ __forceinline__ void exp2_poly2(float& y0, float& y1, float x0, float x1) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932608485221863f;
+  constexpr float kC2 = 0.24261115491390228f, kC3 = 0.05517221987247467f;
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
+  float t0, t1, j0, j1, f0, f1, p0, p1;
+  fadd2(t0, t1, x0, x1, kShift, kShift);
+  fsub2(j0, j1, t0, t1, kShift, kShift);
+  fsub2(f0, f1, x0, x1, j0, j1);
+  ffma2(p0, p1, kC3, kC3, f0, f1, kC2, kC2);
+  ffma2(p0, p1, p0, p1, f0, f1, kC1, kC1);
+  ffma2(p0, p1, p0, p1, f0, f1, kC0, kC0);
+  // the low bits of t hold j; shifting them into the exponent field scales by 2^j
+  y0 = __int_as_float(__float_as_int(t0) * (1 << 23) + __float_as_int(p0));
+  y1 = __int_as_float(__float_as_int(t1) * (1 << 23) + __float_as_int(p1));
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
