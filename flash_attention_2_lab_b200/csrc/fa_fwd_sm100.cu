@@ -121,6 +121,7 @@ struct FwdParams {
   float scale_log2; // softmax scale * log2(e)
   int n_qpairs;     // ceil(ceil(n_q / 128) / 2)
   int n_items;      // bh * n_qpairs
+  int unit;         // work items per scheduling unit (1 or 2)
   unsigned int* status;
   unsigned long long limit_ns;
   float* dbg;       // optional: first item's first masked score tile (tests)
@@ -130,13 +131,27 @@ struct ItemShape {
   int bh, qp, n_t[2], n_max, q0[2];
 };
 
+// Work items are handed out to blocks in units of p.unit consecutive items
+// (block b takes units b, b + grid, b + 2 grid, ...), and every role of a
+// block walks the same sequence.  Units of two are used when there is more
+// than one wave of items; a single wave keeps one item per block.
+#define first_item_of_block() (p.unit * static_cast<int>(blockIdx.x))
+__device__ __forceinline__ int next_item_of(int item, int unit) {
+  if (unit == 1) return item + static_cast<int>(gridDim.x);
+  return (item & 1) ? item - 1 + 2 * static_cast<int>(gridDim.x) : item + 1;
+}
+#define next_item(item) next_item_of(item, p.unit)
+
 __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
   ItemShape s;
   s.bh = item / p.n_qpairs;
-  const int r = item - s.bh * p.n_qpairs;
-  // Causal work grows with the query position: hand out the heaviest pairs of
-  // a head first so the static round-robin schedule ends balanced.
-  s.qp = p.causal ? (p.n_qpairs - 1 - r) : r;
+  const int k = item - s.bh * p.n_qpairs;
+  // Causal work grows with the query position.  Within a head the query
+  // pairs are visited as n-1, 0, n-2, 1, ..., so the two items of a unit (a
+  // pair and its mirror) always add up to the same amount of work and the
+  // static schedule ends balanced.  Both items belong to the same head, which
+  // keeps that head's K/V hot in L2.
+  s.qp = p.causal ? ((k & 1) ? (k >> 1) : (p.n_qpairs - 1 - (k >> 1))) : k;
   const int nkv = (p.n_k + kBlockN - 1) / kBlockN;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
@@ -162,7 +177,7 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
   volatile int* abort_flag = &ctl->abort;
   const uint32_t q_full = smem_u32(&ctl->q_full), q_empty = smem_u32(&ctl->q_empty);
   uint32_t slot = 0, phase = 0;
-  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+  for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item(item, p);
     if (!mbar_wait_warp(q_empty, (q_count & 1) ^ 1, abort_flag, p.status,
                         kStatusTimeoutProducer, p.limit_ns))
@@ -221,13 +236,13 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
     return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutMma, p.limit_ns);
   };
 
-  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+  for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item(item, p);
     if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
     ++q_count;
     tc_fence_after();
     uint32_t v_slot = 0, v_phase = 0;  // ring position of V_{j-1}
-    const bool trace_on = item == static_cast<int>(blockIdx.x) && threadIdx.x % 32 == 0;
+    const bool trace_on = item == first_item_of_block() && threadIdx.x % 32 == 0;
     (void)trace_on;
     for (int j = 0; j <= s.n_max; ++j) {
       TRACE(2, j, 0);
@@ -351,7 +366,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     ++turn_cnt;
   };
 
-  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+  for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item(item, p);
     const int n_t = s.n_t[t];
     if (n_t == 0) {
@@ -366,7 +381,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     float l = 0.f;
 
     for (int j = 0; j < n_t; ++j) {
-      const bool trace_on = item == static_cast<int>(blockIdx.x) && row == 0;
+      const bool trace_on = item == first_item_of_block() && row == 0;
       (void)trace_on;
       TRACE(t, j, 0);
       if (!wait(s_full, s_cnt & 1)) return false;
@@ -393,7 +408,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
         for (int i = 0; i < 128; ++i)
           if (i > lim) sr[i] = __float_as_uint(-INFINITY);
       }
-      if (!FA_TRACE && p.dbg != nullptr && item == static_cast<int>(blockIdx.x) &&
+      if (!FA_TRACE && p.dbg != nullptr && item == first_item_of_block() &&
           blockIdx.x == 0 && j == 0) {
 #pragma unroll
         for (int i = 0; i < 128; ++i) p.dbg[(t * 128 + row) * 128 + i] = __uint_as_float(sr[i]);
@@ -755,7 +770,9 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   p.limit_ns = g_wait_limit_ns;
   p.dbg = dbg;
 
-  const int grid = p.n_items < d->sms ? p.n_items : d->sms;
+  p.unit = p.n_items > d->sms ? 2 : 1;
+  const int units = (p.n_items + p.unit - 1) / p.unit;
+  const int grid = units < d->sms ? units : d->sms;
   fa::fa_fwd_kernel<<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
