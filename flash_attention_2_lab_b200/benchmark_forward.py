@@ -1,0 +1,141 @@
+"""Command-line benchmark of the attention forward, flag-compatible with the
+reference's ``python -m benchmarks.benchmark_forward`` (benchmarks/benchmark_forward.py:24-53)
+and its timing method (benchmarks/harness.py:34-71: warm-up, then samples x
+iterations between CUDA events, median / p10 / p90 per call).
+
+Added columns: TFLOPS (4*B*H*Nq*Nk*D, halved for causal) and the fraction of
+the measured B200 peak.  Added mode: ``--gpus N`` splits the (batch, head)
+slices over N devices of this process and reports the slowest device's time.
+
+    python -m flash_attention_2_lab_b200.benchmark_forward --batch 4 --heads 32 \\
+        --query-length 8192 --causal --dtype float16 --kernels sm100 sdpa
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+from . import attention_forward
+from .sharded import shard_range
+
+DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def percentile(values, fraction):
+    ordered = sorted(values)
+    return ordered[round((len(ordered) - 1) * fraction)]
+
+
+def measured_peak_tflops() -> float:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
+
+
+def time_on_devices(ops, samples, iterations, warmup):
+    """ops: list of (device, callable). Returns per-call ms samples, each the
+    maximum over devices."""
+    for dev, op in ops:
+        with torch.cuda.device(dev):
+            for _ in range(warmup):
+                op()
+    for dev, _ in ops:
+        torch.cuda.synchronize(dev)
+    out = []
+    for _ in range(samples):
+        events = []
+        for dev, op in ops:
+            with torch.cuda.device(dev):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                for _ in range(iterations):
+                    op()
+                e.record()
+                events.append((s, e))
+        for s, e in events:
+            e.synchronize()
+        out.append(max(s.elapsed_time(e) for s, e in events) / iterations)
+    return out
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--heads", type=int, default=8)
+    ap.add_argument("--query-length", type=int, default=512)
+    ap.add_argument("--key-length", type=int, default=None)
+    ap.add_argument("--head-dim", type=int, default=64)
+    ap.add_argument("--causal", action="store_true")
+    ap.add_argument("--dtype", choices=list(DTYPES), default="float16")
+    ap.add_argument("--samples", type=int, default=20)
+    ap.add_argument("--iterations", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=25)
+    ap.add_argument("--kernels", nargs="+", default=None,
+                    help="kernel names: sm100 (this library), sdpa (PyTorch, for context)")
+    ap.add_argument("--gpus", type=int, default=1, help="devices to split (b, h) over")
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args(argv)
+
+    nk = args.key_length if args.key_length is not None else args.query_length
+    dtype = DTYPES[args.dtype]
+    kernels = args.kernels or ["sm100", "sdpa"]
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    q = torch.randn(args.batch, args.heads, args.query_length, args.head_dim, device="cuda",
+                    dtype=dtype, generator=g)
+    k = torch.randn(args.batch, args.heads, nk, args.head_dim, device="cuda", dtype=dtype,
+                    generator=g)
+    v = torch.randn(args.batch, args.heads, nk, args.head_dim, device="cuda", dtype=dtype,
+                    generator=g)
+    flops = 4.0 * args.batch * args.heads * args.query_length * nk * args.head_dim
+    if args.causal:
+        flops /= 2
+    peak = measured_peak_tflops()
+
+    shards = []
+    for r in range(args.gpus):
+        rng = shard_range(args.batch * args.heads, args.gpus, r)
+        dev = torch.device("cuda", r)
+        sl = slice(rng.start, rng.stop)
+        shards.append((dev, *(t.reshape(-1, 1, *t.shape[2:])[sl].transpose(0, 1)
+                              .contiguous().to(dev) for t in (q, k, v))))
+
+    print(f"workload: B={args.batch} H={args.heads} Nq={args.query_length} Nk={nk} "
+          f"D={args.head_dim} causal={args.causal} dtype={args.dtype} gpus={args.gpus}")
+    print(f"{'kernel':10s} {'median ms':>10s} {'p10 ms':>9s} {'p90 ms':>9s} {'TFLOPS':>9s} "
+          f"{'% peak':>7s}")
+    results = {}
+    for name in kernels:
+        if name == "sm100":
+            supported = dtype == torch.float16 and args.head_dim == 64
+            mk = lambda dq, dk, dv: (lambda: attention_forward(dq, dk, dv, args.causal))
+        elif name == "sdpa":
+            supported = True
+            mk = lambda dq, dk, dv: (lambda: F.scaled_dot_product_attention(
+                dq, dk, dv, is_causal=args.causal))
+        else:
+            raise SystemExit(f"unknown kernel {name!r} (choose from sm100, sdpa)")
+        if not supported:
+            print(f"{name:10s} unsupported for this dtype / head dimension")
+            continue
+        ops = [(dev, mk(dq, dk, dv)) for dev, dq, dk, dv in shards]
+        with torch.inference_mode():
+            ms = time_on_devices(ops, args.samples, args.iterations, args.warmup)
+        med = statistics.median(ms)
+        tf = flops / (med / 1e3) / 1e12
+        results[name] = med
+        print(f"{name:10s} {med:10.4f} {percentile(ms, 0.1):9.4f} {percentile(ms, 0.9):9.4f} "
+              f"{tf:9.1f} {100 * tf / (peak * args.gpus):6.1f}%")
+    if "sm100" in results and "sdpa" in results:
+        print(f"sdpa / sm100 time ratio: {results['sdpa'] / results['sm100']:.2f}x")
+
+
+if __name__ == "__main__":
+    main()

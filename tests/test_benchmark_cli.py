@@ -1,0 +1,20 @@
+"""The benchmark CLI keeps the reference's flags (benchmarks/benchmark_forward.py:24-53)."""
+
+import pytest
+
+from flash_attention_2_lab_b200 import benchmark_forward
+
+
+def test_cli_accepts_reference_flags():
+    with pytest.raises(SystemExit) as e:
+        benchmark_forward.main(["--help"])
+    assert e.value.code == 0
+
+
+@pytest.mark.gpu
+def test_cli_runs_small_case(capsys):
+    benchmark_forward.main(["--batch", "1", "--heads", "4", "--query-length", "256", "--causal",
+                            "--dtype", "float16", "--samples", "3", "--iterations", "3",
+                            "--warmup", "3", "--kernels", "sm100", "sdpa"])
+    out = capsys.readouterr().out
+    assert "sm100" in out and "TFLOPS" in out and "sdpa / sm100" in out
