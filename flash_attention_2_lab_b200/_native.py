@@ -28,6 +28,8 @@ ABI = {
     "fa_selftest_wait_timeout": (_int, [ctypes.c_ulonglong, _vp]),
     "fa_smem_bytes": (_int, []),
     "fa_fwd_sm100_debug": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _f32, _vp, _vp]),
+    "fa_set_max_splits": (None, [_int]),
+    "fa_release_workspaces": (_int, []),
 }
 
 _lib = None

@@ -42,7 +42,9 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "sm100_ptx.cuh"
 #include "fa_sm100.h"
@@ -107,9 +109,11 @@ struct SharedCtl {
   uint64_t kv_full[kKvSlots], kv_empty[kKvSlots];
   uint64_t s_full[2], s_empty[2], p_full[2], o_done[2], o_empty[2];
   uint64_t exp_turn[2];  // alternates the two softmax warpgroups' exponential phases
+  uint64_t wg_bar[2];    // a tile's four softmax warps (key-range split epilogue)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int merge_flag[2];
 };
 static_assert(sizeof(SharedCtl) <= kSmemCtlBytes, "control block too large");
 
@@ -125,10 +129,23 @@ struct FwdParams {
   unsigned int* status;
   unsigned long long limit_ns;
   float* dbg;       // optional: first item's first masked score tile (tests)
+  // Key-range split (n_split > 1): a work item is (bh, query pair, split);
+  // each split writes fp32 partial results and the last split to finish a
+  // query tile merges them.  The three arrays live in one scratch buffer.
+  int n_split;      // splits of the key range per query pair (1 = no split)
+  int kv_chunk;     // key tiles per split
+  int n_qtiles;     // ceil(n_q / 128)
+  float* part_o;    // [bh][n_qtiles][n_split][128][64] partial numerators
+  float2* part_ml;  // [bh][n_qtiles][n_split][128] (max used, partial sum)
+  int* counters;    // [bh][n_qtiles] finished splits; reset to 0 by the merging block
+  __half* out;      // o, for the merge's direct stores
 };
 
+// Key tiles [jb, n_t[t]) of query tile t belong to the item (n_t[t] <= jb:
+// none); n_max = max(n_t).  valid[t]: the query tile exists.
 struct ItemShape {
-  int bh, qp, n_t[2], n_max, q0[2];
+  int bh, qp, split, jb, n_t[2], n_max, q0[2];
+  bool valid[2];
 };
 
 // Work items are handed out to blocks in units of p.unit consecutive items
@@ -144,26 +161,40 @@ __device__ __forceinline__ int next_item_of(int item, int unit) {
 
 __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
   ItemShape s;
-  s.bh = item / p.n_qpairs;
-  const int k = item - s.bh * p.n_qpairs;
+  int k;
+  if (p.n_split > 1) {
+    s.split = item % p.n_split;
+    const int pair = item / p.n_split;
+    s.bh = pair / p.n_qpairs;
+    k = pair - s.bh * p.n_qpairs;
+  } else {
+    s.split = 0;
+    s.bh = item / p.n_qpairs;
+    k = item - s.bh * p.n_qpairs;
+  }
   // Causal work grows with the query position.  Within a head the query
   // pairs are visited as n-1, 0, n-2, 1, ..., so the two items of a unit (a
   // pair and its mirror) always add up to the same amount of work and the
   // static schedule ends balanced.  Both items belong to the same head, which
   // keeps that head's K/V hot in L2.
-  s.qp = p.causal ? ((k & 1) ? (k >> 1) : (p.n_qpairs - 1 - (k >> 1))) : k;
+  s.qp = (p.causal && p.n_split == 1) ? ((k & 1) ? (k >> 1) : (p.n_qpairs - 1 - (k >> 1))) : k;
   const int nkv = (p.n_k + kBlockN - 1) / kBlockN;
+  s.jb = s.split * p.kv_chunk;
+  const int je = s.jb + p.kv_chunk;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     s.q0[t] = s.qp * 2 * kBlockM + t * kBlockM;
-    if (s.q0[t] >= p.n_q) {
-      s.n_t[t] = 0;
+    s.valid[t] = s.q0[t] < p.n_q;
+    int n = 0;
+    if (!s.valid[t]) {
+      n = 0;
     } else if (p.causal) {
       const int diag = s.q0[t] / kBlockN + 1;  // tiles up to and including the diagonal
-      s.n_t[t] = diag < nkv ? diag : nkv;
+      n = diag < nkv ? diag : nkv;
     } else {
-      s.n_t[t] = nkv;
+      n = nkv;
     }
+    s.n_t[t] = n < je ? n : je;
   }
   s.n_max = s.n_t[0] > s.n_t[1] ? s.n_t[0] : s.n_t[1];
   return s;
@@ -179,10 +210,11 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
   uint32_t slot = 0, phase = 0;
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item(item, p);
+    if (s.n_max <= s.jb) continue;  // no key tiles in this item
     if (!mbar_wait_warp(q_empty, (q_count & 1) ^ 1, abort_flag, p.status,
                         kStatusTimeoutProducer, p.limit_ns))
       return false;
-    const uint32_t nq = (s.n_t[1] > 0) ? 2 : 1;
+    const uint32_t nq = (s.n_t[1] > s.jb) ? 2 : 1;
     if (elect_one()) {
       mbar_arrive_expect_tx(q_full, nq * kTileBytes);
       tma_load_3d(smem_base + kSmemQ, tm_q, q_full, 0, s.q0[0], s.bh);
@@ -190,7 +222,7 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
     }
     __syncwarp();
     ++q_count;
-    for (int j = 0; j < s.n_max; ++j) {
+    for (int j = s.jb; j < s.n_max; ++j) {
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         if (!mbar_wait_warp(smem_u32(&ctl->kv_empty[slot]), phase ^ 1, abort_flag, p.status,
@@ -238,13 +270,14 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
 
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item(item, p);
+    if (s.n_max <= s.jb) continue;  // no key tiles in this item
     if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
     ++q_count;
     tc_fence_after();
     uint32_t v_slot = 0, v_phase = 0;  // ring position of V_{j-1}
     const bool trace_on = item == first_item_of_block() && threadIdx.x % 32 == 0;
     (void)trace_on;
-    for (int j = 0; j <= s.n_max; ++j) {
+    for (int j = s.jb; j <= s.n_max; ++j) {
       TRACE(2, j, 0);
       uint32_t next_v_slot = 0, next_v_phase = 0;
       if (j < s.n_max) {
@@ -284,7 +317,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
         }
         __syncwarp();
       }
-      if (j > 0) {
+      if (j > s.jb) {
         // ---- O_t += P_t V_{j-1}
         const int jj = j - 1;
         if (!wait(smem_u32(&ctl->kv_full[v_slot]), v_phase)) return false;
@@ -294,7 +327,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (jj >= s.n_t[t]) continue;
-          if (jj == 0) {
+          if (jj == s.jb) {
             // O_t is overwritten by this item's first PV: the previous item's
             // epilogue must have read it.
             if (!wait(smem_u32(&ctl->o_empty[t]), (o_cnt[t] & 1) ^ 1)) return false;
@@ -309,7 +342,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
             for (int kk = 0; kk < kBlockN / 16; ++kk) {
               // P: 16 keys = 8 packed columns per step; V: 16 key rows = 2 KiB.
               mma_ts_f16(tmem + col_o(t), tmem + col_p(t) + kk * 8, dv + 128 * kk, idesc_pv,
-                         (jj > 0 || kk > 0) ? 1u : 0u);
+                         (jj > s.jb || kk > 0) ? 1u : 0u);
             }
             tc_commit(smem_u32(&ctl->o_done[t]));
           }
@@ -343,7 +376,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   const uint32_t stage = smem_base + kSmemO + t * kTileBytes;
   const float c = p.scale_log2;
   const bool leader = (row == 0);
-  uint32_t s_cnt = 0, od_cnt = 0;
+  uint32_t s_cnt = 0, od_cnt = 0, wg_cnt = 0;
   bool first_item = true;
 
   auto wait = [&](uint32_t bar, uint32_t parity) {
@@ -366,13 +399,94 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     ++turn_cnt;
   };
 
+  // Key-range split epilogue: store this split's partial result (numerator
+  // rows `orr`, or none for an empty range, with the max used and the partial
+  // sum), count the split as finished, and let the last split of the query
+  // tile merge all partials into o.
+  auto split_epilogue = [&](const ItemShape& s, const uint32_t* orr, float m, float lsum) {
+    const int qtile = s.q0[t] / kBlockM;
+    const size_t tile_idx = static_cast<size_t>(s.bh) * p.n_qtiles + qtile;
+    const size_t part = (tile_idx * p.n_split + s.split) * kBlockM + row;
+    if (orr != nullptr) {
+      float4* dst = reinterpret_cast<float4*>(p.part_o + part * kHeadDim);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        dst[i] = make_float4(__uint_as_float(orr[4 * i]), __uint_as_float(orr[4 * i + 1]),
+                             __uint_as_float(orr[4 * i + 2]), __uint_as_float(orr[4 * i + 3]));
+    }
+    p.part_ml[part] = make_float2(m, lsum);
+    __threadfence();
+    const uint32_t wg_bar = smem_u32(&ctl->wg_bar[t]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(wg_bar);
+    if (!wait(wg_bar, wg_cnt & 1)) return false;
+    ++wg_cnt;
+    if (row == 0) {
+      const int done = atomicAdd(p.counters + tile_idx, 1) + 1;
+      const int last = done == p.n_split ? 1 : 0;
+      if (last) {
+        atomicExch(p.counters + tile_idx, 0);  // ready for the next launch
+        __threadfence();
+      }
+      ctl->merge_flag[t] = last;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(wg_bar);
+    if (!wait(wg_bar, wg_cnt & 1)) return false;
+    ++wg_cnt;
+    if (!*reinterpret_cast<volatile int*>(&ctl->merge_flag[t])) return true;
+    // ---- merge: o = sum_s w_s O_s / sum_s w_s l_s, w_s = 2^((m_s - max m) * c)
+    const size_t base = tile_idx * p.n_split * kBlockM + row;
+    float mmax = -INFINITY;
+    for (int sp = 0; sp < p.n_split; ++sp) {
+      const float2 ml = __ldcg(p.part_ml + base + static_cast<size_t>(sp) * kBlockM);
+      if (ml.y > 0.f) mmax = fmaxf(mmax, ml.x);
+    }
+    float acc[kHeadDim];
+#pragma unroll
+    for (int i = 0; i < kHeadDim; ++i) acc[i] = 0.f;
+    float den = 0.f;
+    for (int sp = 0; sp < p.n_split; ++sp) {
+      const size_t pi = base + static_cast<size_t>(sp) * kBlockM;
+      const float2 ml = __ldcg(p.part_ml + pi);
+      if (!(ml.y > 0.f)) continue;
+      const float w = ex2_approx((ml.x - mmax) * c);
+      den = fmaf(w, ml.y, den);
+      const float4* src = reinterpret_cast<const float4*>(p.part_o + pi * kHeadDim);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 v = __ldcg(src + i);
+        acc[4 * i] = fmaf(w, v.x, acc[4 * i]);
+        acc[4 * i + 1] = fmaf(w, v.y, acc[4 * i + 1]);
+        acc[4 * i + 2] = fmaf(w, v.z, acc[4 * i + 2]);
+        acc[4 * i + 3] = fmaf(w, v.w, acc[4 * i + 3]);
+      }
+    }
+    const int qr = s.q0[t] + row;
+    if (qr < p.n_q) {
+      const float inv = 1.f / den;
+      uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(s.bh) * p.n_q + qr) *
+                                                        kHeadDim);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        dst[i] = make_uint4(pack_half2(acc[8 * i] * inv, acc[8 * i + 1] * inv),
+                            pack_half2(acc[8 * i + 2] * inv, acc[8 * i + 3] * inv),
+                            pack_half2(acc[8 * i + 4] * inv, acc[8 * i + 5] * inv),
+                            pack_half2(acc[8 * i + 6] * inv, acc[8 * i + 7] * inv));
+    }
+    return true;
+  };
+
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item(item, p);
     const int n_t = s.n_t[t];
-    if (n_t == 0) {
-      for (int j = 0; j < s.n_max; ++j) {
+    if (n_t <= s.jb) {
+      for (int j = s.jb; j < s.n_max; ++j) {
         if (!take_turn()) return false;
         pass_turn();
+      }
+      if (p.n_split > 1 && s.valid[t]) {
+        if (!split_epilogue(s, nullptr, -INFINITY, 0.f)) return false;
       }
       continue;
     }
@@ -380,7 +494,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     float m_used = -INFINITY;
     float l = 0.f;
 
-    for (int j = 0; j < n_t; ++j) {
+    for (int j = s.jb; j < n_t; ++j) {
       const bool trace_on = item == first_item_of_block() && row == 0;
       (void)trace_on;
       TRACE(t, j, 0);
@@ -464,7 +578,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       l += ((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7]));
       TRACE(t, j, 4);
 
-      if (j > 0) {
+      if (j > s.jb) {
         // PV(j-1) must be done before P_t is overwritten or O_t is rescaled.
         if (!wait(o_done, od_cnt & 1)) return false;
         ++od_cnt;
@@ -512,6 +626,10 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(o_empty);
+    if (p.n_split > 1) {
+      if (!split_epilogue(s, orr, m_used, l)) return false;
+      continue;
+    }
 
     const float inv = 1.f / l;
     uint32_t h[32];
@@ -566,6 +684,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&ctl->o_done[t]), 1);
       mbar_init(smem_u32(&ctl->o_empty[t]), 4);
       mbar_init(smem_u32(&ctl->exp_turn[t]), 4);
+      mbar_init(smem_u32(&ctl->wg_bar[t]), 4);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
@@ -678,6 +797,94 @@ struct DeviceState {
 DeviceState g_dev[kMaxDevices];
 EncodeTiledFn g_encode = nullptr;
 std::mutex g_mutex;
+int g_max_splits = 0;  // 0: automatic, 1: never split the key range, k: at most k splits
+
+// Scratch of the key-range split mode, one buffer per (device, stream) so
+// launches on different streams never share it; launches on one stream are
+// ordered.  Allocated on first need, grown when a larger problem arrives, and
+// held until fa_release_workspaces().
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, Workspace> g_workspaces;
+
+// How a launch splits the key range, and the scratch that needs.
+struct SplitPlan {
+  int n_split = 1, kv_chunk = 0, n_qtiles = 0;
+  size_t counters_bytes = 0, ml_bytes = 0, o_bytes = 0;
+  size_t total() const { return counters_bytes + ml_bytes + o_bytes; }
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// The split counters occupy a fixed prefix of every scratch buffer, whatever
+// the problem, so the partial results of one launch never land where another
+// launch's counters live: the kernel leaves every counter it uses at zero and
+// nothing else writes to the prefix.
+constexpr size_t kMaxSplitTiles = 1024;
+constexpr size_t kCounterBytes = kMaxSplitTiles * sizeof(int);
+
+SplitPlan plan_split(int64_t bh, int64_t n_q, int64_t n_k, int sms) {
+  SplitPlan sp;
+  const int64_t n_qpairs = ((n_q + 127) / 128 + 1) / 2;
+  const int64_t pairs = bh * n_qpairs;
+  const int64_t nkv = (n_k + 127) / 128;
+  sp.n_qtiles = static_cast<int>((n_q + 127) / 128);
+  sp.kv_chunk = static_cast<int>(nkv);
+  // Split only when the query pairs leave SMs idle, and keep >= 8 key tiles
+  // per split: a block's fixed cost (Q load, pipeline fill, partial write and
+  // merge) is worth a few key tiles, so shorter splits measured slower than
+  // no split on a B200.
+  if (g_max_splits != 1 && pairs < sms) {
+    int64_t want = sms / pairs;
+    const int64_t cap = nkv / 8;
+    if (want > cap) want = cap;
+    if (g_max_splits > 1 && want > g_max_splits) want = g_max_splits;
+    if (want >= 2) {
+      sp.kv_chunk = static_cast<int>((nkv + want - 1) / want);
+      sp.n_split = static_cast<int>((nkv + sp.kv_chunk - 1) / sp.kv_chunk);
+    }
+  }
+  if (sp.n_split > 1 && static_cast<size_t>(bh) * sp.n_qtiles > kMaxSplitTiles) {
+    sp.n_split = 1;
+    sp.kv_chunk = static_cast<int>(nkv);
+  }
+  if (sp.n_split > 1) {
+    const size_t tiles = static_cast<size_t>(bh) * sp.n_qtiles;
+    sp.counters_bytes = kCounterBytes;
+    sp.ml_bytes = align256(tiles * sp.n_split * 128 * sizeof(float2));
+    sp.o_bytes = tiles * sp.n_split * 128 * 64 * sizeof(float);
+  }
+  return sp;
+}
+
+int get_workspace(int dev, cudaStream_t stream, size_t need, void** out) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  Workspace& w = g_workspaces[std::make_pair(dev, stream)];
+  if (w.bytes < need) {
+    cudaError_t e = cudaSuccess;
+    if (w.ptr != nullptr) {
+      e = cudaStreamSynchronize(stream);
+      if (e == cudaSuccess) e = cudaFree(w.ptr);
+      w.ptr = nullptr;
+      w.bytes = 0;
+      if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "workspace release: %s", cudaGetErrorString(e));
+    }
+    e = cudaMalloc(&w.ptr, need);
+    if (e != cudaSuccess) {
+      w.ptr = nullptr;
+      return set_error(FA_ERR_CUDA, "workspace allocation (%zu bytes): %s", need,
+                       cudaGetErrorString(e));
+    }
+    w.bytes = need;
+    // the split counters must start at zero; the kernel leaves them at zero
+    e = cudaMemsetAsync(w.ptr, 0, need, stream);
+    if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "workspace clear: %s", cudaGetErrorString(e));
+  }
+  *out = w.ptr;
+  return FA_OK;
+}
 
 int ensure_device(int dev, DeviceState** out) {
   if (dev < 0 || dev >= kMaxDevices) return set_error(FA_ERR_CUDA, "device index %d out of range", dev);
@@ -770,7 +977,25 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   p.limit_ns = g_wait_limit_ns;
   p.dbg = dbg;
 
-  p.unit = p.n_items > d->sms ? 2 : 1;
+  p.out = static_cast<__half*>(o);
+  const SplitPlan sp = plan_split(bh, n_q, n_k, d->sms);
+  p.n_split = sp.n_split;
+  p.kv_chunk = sp.kv_chunk;
+  p.n_qtiles = sp.n_qtiles;
+  p.part_o = nullptr;
+  p.part_ml = nullptr;
+  p.counters = nullptr;
+  if (sp.n_split > 1) {
+    void* ws = nullptr;
+    if ((rc = get_workspace(dev, stream, sp.total(), &ws)) != FA_OK) return rc;
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    p.counters = reinterpret_cast<int*>(base);
+    p.part_ml = reinterpret_cast<float2*>(base + sp.counters_bytes);
+    p.part_o = reinterpret_cast<float*>(base + sp.counters_bytes + sp.ml_bytes);
+    p.n_items *= sp.n_split;
+  }
+
+  p.unit = (p.n_split == 1 && p.n_items > d->sms) ? 2 : 1;
   const int units = (p.n_items + p.unit - 1) / p.unit;
   const int grid = units < d->sms ? units : d->sms;
   fa::fa_fwd_kernel<<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
@@ -847,5 +1072,24 @@ int fa_selftest_wait_timeout(unsigned long long limit_ns, void* cuda_stream) {
 }
 
 int fa_smem_bytes(void) { return static_cast<int>(fa::kSmemBytes); }
+
+void fa_set_max_splits(int max_splits) { g_max_splits = max_splits < 0 ? 0 : max_splits; }
+
+int fa_release_workspaces(void) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  int rc = FA_OK;
+  for (auto& kv : g_workspaces) {
+    if (kv.second.ptr == nullptr) continue;
+    cudaError_t e = cudaSetDevice(kv.first.first);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaFree(kv.second.ptr);
+    if (e != cudaSuccess) rc = set_error(FA_ERR_CUDA, "workspace release: %s", cudaGetErrorString(e));
+  }
+  g_workspaces.clear();
+  cudaSetDevice(prev);
+  return rc;
+}
 
 }  // extern "C"

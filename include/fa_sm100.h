@@ -78,6 +78,22 @@ int fa_selftest_wait_timeout(unsigned long long limit_ns, void* cuda_stream);
 int fa_smem_bytes(void);
 
 /*
+ * Key-range split policy for problems with fewer query pairs than SMs:
+ * 0 = automatic (default), 1 = never split, k > 1 = at most k splits. In split
+ * mode each split writes an fp32 partial result to a scratch buffer and the
+ * last split to finish a query tile merges them; the scratch is one buffer per
+ * (device, stream), allocated on first need and kept for reuse.
+ * No counterpart in the reference (its grid never splits the key range).
+ */
+void fa_set_max_splits(int max_splits);
+
+/*
+ * Synchronises every device that holds a split-mode scratch buffer and frees
+ * them all. No counterpart in the reference.
+ */
+int fa_release_workspaces(void);
+
+/*
  * Test hook: as fa_fwd_sm100, and additionally writes the first work item's
  * first masked score tile (256 x 128 fp32, raw Q K^T before scaling) to
  * score_dump. Used only by the tests to localise layout errors.
