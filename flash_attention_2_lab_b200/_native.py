@@ -22,6 +22,7 @@ _i64, _vp, _int, _f32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_
 ABI = {
     "fa_fwd_sm100": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _f32, _vp]),
     "fa_fwd_sm100_varlen": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _f32, _vp]),
+    "fa_fwd_sm100_noalloc": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _f32, _vp]),
     "fa_last_error": (ctypes.c_char_p, []),
     "fa_read_status": (_int, [_vp, ctypes.POINTER(ctypes.c_uint), _int]),
     "fa_set_wait_limit_ns": (None, [ctypes.c_ulonglong]),

@@ -767,6 +767,13 @@ __global__ void selftest_timeout_kernel(unsigned int* status, unsigned long long
 
 __device__ unsigned int g_status_word;
 
+// Scratch of fa_fwd_sm100_noalloc: a fixed array that exists on every device
+// that loads this library, for callers that cannot allocate.  12 MiB covers
+// the largest key-range split plan on a 148-SM B200 (at most ~296 partial
+// query tiles of 33 KiB plus the counter prefix).
+constexpr size_t kNoAllocScratchBytes = 12u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
 }  // namespace fa
 
 // ====================================================================== host
@@ -793,6 +800,7 @@ struct DeviceState {
   bool ready = false;
   int sms = 0;
   unsigned int* status = nullptr;
+  void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch
 };
 DeviceState g_dev[kMaxDevices];
 EncodeTiledFn g_encode = nullptr;
@@ -917,6 +925,14 @@ int ensure_device(int dev, DeviceState** out) {
     if (e != cudaSuccess)
       return set_error(FA_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
     d.status = static_cast<unsigned int*>(sym);
+    // In host code g_noalloc_scratch names a host-side shadow, not device
+    // memory: the device address is looked up here, once per device, with
+    // that device current.
+    void* scratch = nullptr;
+    e = cudaGetSymbolAddress(&scratch, fa::g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_error(FA_ERR_CUDA, "cudaGetSymbolAddress (scratch): %s", cudaGetErrorString(e));
+    d.noalloc_scratch = scratch;
     d.ready = true;
   }
   *out = &d;
@@ -937,7 +953,8 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t slices) {
 }
 
 int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int64_t n_q,
-           int64_t n_k, int causal, float scale, cudaStream_t stream, float* dbg) {
+           int64_t n_k, int causal, float scale, cudaStream_t stream, float* dbg,
+           bool noalloc = false) {
   if (bh < 0 || n_q < 0 || n_k < 0) return set_error(FA_ERR_INVALID, "negative size");
   if (bh == 0 || n_q == 0) return FA_OK;
   if (n_k == 0) return set_error(FA_ERR_INVALID, "key length must be positive when queries exist");
@@ -987,7 +1004,21 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   p.counters = nullptr;
   if (sp.n_split > 1) {
     void* ws = nullptr;
-    if ((rc = get_workspace(dev, stream, sp.total(), &ws)) != FA_OK) return rc;
+    if (noalloc) {
+      if (sp.total() > fa::kNoAllocScratchBytes)
+        return set_error(FA_ERR_INVALID,
+                         "this problem needs %zu bytes of scratch; fa_fwd_sm100_noalloc holds "
+                         "at most %zu",
+                         sp.total(), static_cast<size_t>(fa::kNoAllocScratchBytes));
+      ws = d->noalloc_scratch;
+      // the split counters must start at zero (a call that timed out could
+      // have left some set); clearing is not an allocation
+      e = cudaMemsetAsync(ws, 0, sp.counters_bytes, stream);
+      if (e != cudaSuccess)
+        return set_error(FA_ERR_CUDA, "scratch clear: %s", cudaGetErrorString(e));
+    } else if ((rc = get_workspace(dev, stream, sp.total(), &ws)) != FA_OK) {
+      return rc;
+    }
     uint8_t* base = static_cast<uint8_t*>(ws);
     p.counters = reinterpret_cast<int*>(base);
     p.part_ml = reinterpret_cast<float2*>(base + sp.counters_bytes);
@@ -1021,6 +1052,14 @@ int fa_fwd_sm100_varlen(const void* q, const void* k, const void* v, void* o, in
   if (batch < 0 || heads < 0) return set_error(FA_ERR_INVALID, "negative size");
   return launch(q, k, v, o, batch * heads, q_len, kv_len, causal, scale,
                 static_cast<cudaStream_t>(cuda_stream), nullptr);
+}
+
+int fa_fwd_sm100_noalloc(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                         int64_t heads, int64_t q_len, int64_t kv_len, int causal, float scale,
+                         void* cuda_stream) {
+  if (batch < 0 || heads < 0) return set_error(FA_ERR_INVALID, "negative size");
+  return launch(q, k, v, o, batch * heads, q_len, kv_len, causal, scale,
+                static_cast<cudaStream_t>(cuda_stream), nullptr, /*noalloc=*/true);
 }
 
 int fa_fwd_sm100_debug(const void* q, const void* k, const void* v, void* o, int64_t batch,

@@ -52,6 +52,29 @@ int fa_fwd_sm100_varlen(const void* q, const void* k, const void* v, void* o, in
                         int64_t heads, int64_t q_len, int64_t kv_len, int causal, float scale,
                         void* cuda_stream);
 
+/*
+ * Same computation as fa_fwd_sm100_varlen, for callers that must not allocate
+ * device memory during the call: code that runs while a CUDA graph is being
+ * captured (an allocation there breaks the capture), serving paths that work
+ * within a memory budget fixed at start-up, and code called from inside an
+ * allocator or memory-pool callback. fa_fwd_sm100_varlen allocates a scratch
+ * buffer per stream the first time a problem uses the key-range split mode;
+ * this entry point instead uses one fixed 12 MiB array compiled into the
+ * library, which every GPU that loads the library holds until the process
+ * exits, and calls no cudaMalloc or cudaFree. A problem whose split plan needs
+ * more scratch than that is rejected with FA_ERR_INVALID and a message giving
+ * both sizes. The caller still provides q, k, v and o.
+ * The array is shared by every call on a device and keeps the last call's
+ * contents (its counters are cleared at the start of each call): calls that
+ * overlap on the GPU, e.g. on two streams, race and must not be made.
+ * The first call into this library on a device looks up the array's device
+ * address; make that first call before any stream capture.
+ * No counterpart in the reference.
+ */
+int fa_fwd_sm100_noalloc(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                         int64_t heads, int64_t q_len, int64_t kv_len, int causal, float scale,
+                         void* cuda_stream);
+
 /* Message for the last failing call on this thread ("" if none). */
 const char* fa_last_error(void);
 
