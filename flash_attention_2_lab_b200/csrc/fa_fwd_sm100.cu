@@ -103,6 +103,10 @@ constexpr unsigned int kStatusTimeoutMma = 1u << 1;
 constexpr unsigned int kStatusTimeoutSoftmax = 1u << 2;
 constexpr unsigned int kStatusTimeoutDrain = 1u << 3;
 constexpr unsigned int kStatusTimeoutSelftest = 1u << 4;
+// Waits for this block's own copies and MMAs before it exits use their own
+// limit, independent of the caller's, so a short limit cannot make a block
+// leave with work in flight (those complete within microseconds).
+constexpr unsigned long long kDrainLimitNs = 200000000ull;
 
 struct SharedCtl {
   uint64_t q_full, q_empty;
@@ -399,6 +403,17 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     ++turn_cnt;
   };
 
+  // Barrier of the tile's four softmax warps, bounded like every other wait
+  // (a named barrier would wait forever for a warp that gave up).
+  auto wg_sync = [&]() {
+    const uint32_t bar = smem_u32(&ctl->wg_bar[t]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+    const bool ok = wait(bar, wg_cnt & 1);
+    ++wg_cnt;
+    return ok;
+  };
+
   // Key-range split epilogue: store this split's partial result (numerator
   // rows `orr`, or none for an empty range, with the max used and the partial
   // sum), count the split as finished, and let the last split of the query
@@ -416,11 +431,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     }
     p.part_ml[part] = make_float2(m, lsum);
     __threadfence();
-    const uint32_t wg_bar = smem_u32(&ctl->wg_bar[t]);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(wg_bar);
-    if (!wait(wg_bar, wg_cnt & 1)) return false;
-    ++wg_cnt;
+    if (!wg_sync()) return false;
     if (row == 0) {
       const int done = atomicAdd(p.counters + tile_idx, 1) + 1;
       const int last = done == p.n_split ? 1 : 0;
@@ -430,10 +441,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       }
       ctl->merge_flag[t] = last;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(wg_bar);
-    if (!wait(wg_bar, wg_cnt & 1)) return false;
-    ++wg_cnt;
+    if (!wg_sync()) return false;
     if (!*reinterpret_cast<volatile int*>(&ctl->merge_flag[t])) return true;
     // ---- merge: o = sum_s w_s O_s / sum_s w_s l_s, w_s = 2^((m_s - max m) * c)
     const size_t base = tile_idx * p.n_split * kBlockM + row;
@@ -638,7 +646,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       h[i] = pack_half2(__uint_as_float(orr[2 * i]) * inv, __uint_as_float(orr[2 * i + 1]) * inv);
 
     if (leader && !first_item) bulk_wait_group_read0();
-    named_bar_sync(1 + t, 128);
+    if (!wg_sync()) return false;
     const uint32_t row_addr = stage + row * 128;
 #pragma unroll
     for (int ch = 0; ch < 8; ++ch) {
@@ -648,7 +656,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
                    : "memory");
     }
     fence_proxy_async_smem();
-    named_bar_sync(1 + t, 128);
+    if (!wg_sync()) return false;
     if (leader) {
       tma_store_3d(tm_o, stage, 0, s.q0[t], s.bh);
       bulk_commit_group();
@@ -724,11 +732,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (uint32_t i = 0; i < n; ++i) {
         const uint32_t idx = ld_count - 1 - i;
         mbar_wait(smem_u32(&ctl->kv_full[idx % kKvSlots]), (idx / kKvSlots) & 1, nullptr,
-                  p.status, kStatusTimeoutDrain, p.limit_ns);
+                  p.status, kStatusTimeoutDrain, kDrainLimitNs);
       }
       if (q_count > 0)
         mbar_wait(smem_u32(&ctl->q_full), (q_count - 1) & 1, nullptr, p.status,
-                  kStatusTimeoutDrain, p.limit_ns);
+                  kStatusTimeoutDrain, kDrainLimitNs);
     }
     __syncwarp();
   } else if (warp == 9) {
@@ -737,7 +745,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // before tensor memory and shared memory are released.
     if (lane == 0) {
       tc_commit(smem_u32(&ctl->drain));
-      mbar_wait(smem_u32(&ctl->drain), 0, nullptr, p.status, kStatusTimeoutDrain, p.limit_ns);
+      mbar_wait(smem_u32(&ctl->drain), 0, nullptr, p.status, kStatusTimeoutDrain, kDrainLimitNs);
     }
     __syncwarp();
   }
