@@ -127,7 +127,9 @@ struct FwdParams {
   int bh;           // batch * heads
   int causal;       // top-left aligned: key index > query index is masked
   float scale_log2; // softmax scale * log2(e)
-  int n_qpairs;     // ceil(ceil(n_q / 128) / 2)
+  int n_qpairs;     // work items per (batch, head) and split: ceil(ceil(n_q / 128) / 2),
+                    // or ceil(n_q / 128) when `single`
+  int single;       // 1: a work item is one 128-row query tile (short problems)
   int n_items;      // bh * n_qpairs
   int unit;         // work items per scheduling unit (1 or 2)
   unsigned int* status;
@@ -187,7 +189,7 @@ __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
   const int je = s.jb + p.kv_chunk;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    s.q0[t] = s.qp * 2 * kBlockM + t * kBlockM;
+    s.q0[t] = p.single ? (t == 0 ? s.qp * kBlockM : p.n_q) : s.qp * 2 * kBlockM + t * kBlockM;
     s.valid[t] = s.q0[t] < p.n_q;
     int n = 0;
     if (!s.valid[t]) {
@@ -1034,6 +1036,15 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
     p.n_items *= sp.n_split;
   }
 
+  // Short problems: when the query pairs would fill at most half the SMs,
+  // make every 128-row query tile its own work item (twice the blocks; a
+  // block's second tile only adds serial work there).
+  p.single = 0;
+  if (p.n_split == 1 && 2 * static_cast<int64_t>(p.n_items) <= d->sms) {
+    p.single = 1;
+    p.n_qpairs = sp.n_qtiles;
+    p.n_items = static_cast<int>(bh * sp.n_qtiles);
+  }
   p.unit = (p.n_split == 1 && p.n_items > d->sms) ? 2 : 1;
   const int units = (p.n_items + p.unit - 1) / p.unit;
   const int grid = units < d->sms ? units : d->sms;
