@@ -398,8 +398,15 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   const uint32_t turn_mine = smem_u32(&ctl->exp_turn[t]);
   const uint32_t turn_other = smem_u32(&ctl->exp_turn[t ^ 1]);
   uint32_t turn_cnt = 0;
-  auto take_turn = [&]() { return wait(turn_mine, (turn_cnt & 1) ^ (t == 0 ? 1u : 0u)); };
+  // Turns are taken only in items where both tiles have key tiles; a lone
+  // tile runs freely.
+  bool use_turns = true;
+  auto take_turn = [&]() {
+    if (!use_turns) return true;
+    return wait(turn_mine, (turn_cnt & 1) ^ (t == 0 ? 1u : 0u));
+  };
   auto pass_turn = [&]() {
+    if (!use_turns) return;
     __syncwarp();
     if (lane == 0) mbar_arrive(turn_other);
     ++turn_cnt;
@@ -490,6 +497,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item(item, p);
     const int n_t = s.n_t[t];
+    use_turns = s.n_t[0] > s.jb && s.n_t[1] > s.jb;
     if (n_t <= s.jb) {
       for (int j = s.jb; j < s.n_max; ++j) {
         if (!take_turn()) return false;
