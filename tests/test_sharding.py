@@ -87,3 +87,33 @@ def test_gloo_world2_sharded_equals_full(tmp_path):
 
 def test_max_over_ranks_without_process_group():
     assert max_over_ranks(3.5) == 3.5
+
+
+def _rank_dies(rank, world, port, result_dir):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        os._exit(0)  # a rank that leaves between steps, before the timing reduction
+    try:
+        max_over_ranks(1.0)
+        outcome = "returned"
+    except Exception as e:  # the surviving rank must get an error, not hang
+        outcome = "error: " + type(e).__name__
+    with open(os.path.join(result_dir, "outcome.txt"), "w") as f:
+        f.write(outcome)
+    os._exit(0)
+
+
+def test_lost_rank_is_detected_not_hung(tmp_path):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_rank_dies, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+        assert not p.is_alive()
+    assert (tmp_path / "outcome.txt").read_text().startswith("error")
