@@ -22,7 +22,8 @@
 //   O_t  128 x  64 fp32   (columns 256 / 320)
 //   P_t  128 x 128 fp16   (columns 384 / 448, two halves per column)
 // so the MMA warp can compute S_t(j+1) while the softmax warps are still
-// turning S_t(j) into P_t(j).  The two softmax warpgroups take turns on the
+// turning S_t(j) into P_t(j).  Each softmax warp writes its 32 rows of the
+// normalised output with its own TMA store.  The two softmax warpgroups take turns on the
 // MUFU (16 ex2/clk/SM, the unit that bounds attention at head dimension 64):
 // one tile's exponentials overlap the other tile's S load, row max and P
 // store.
@@ -171,10 +172,11 @@ __device__ __forceinline__ int next_item_of(int item, int unit) {
 }
 #define next_item(item) next_item_of(item, p.unit)
 
+template <bool kSplit>
 __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
   ItemShape s;
   int k;
-  if (p.n_split > 1) {
+  if (kSplit) {
     s.split = item % p.n_split;
     const int pair = item / p.n_split;
     s.bh = pair / p.n_qpairs;
@@ -189,10 +191,10 @@ __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
   // pair and its mirror) always add up to the same amount of work and the
   // static schedule ends balanced.  Both items belong to the same head, which
   // keeps that head's K/V hot in L2.
-  s.qp = (p.causal && p.n_split == 1) ? ((k & 1) ? (k >> 1) : (p.n_qpairs - 1 - (k >> 1))) : k;
+  s.qp = (p.causal && !kSplit) ? ((k & 1) ? (k >> 1) : (p.n_qpairs - 1 - (k >> 1))) : k;
   const int nkv = (p.n_k + kBlockN - 1) / kBlockN;
-  s.jb = s.split * p.kv_chunk;
-  const int je = s.jb + p.kv_chunk;
+  s.jb = kSplit ? s.split * p.kv_chunk : 0;
+  const int je = kSplit ? s.jb + p.kv_chunk : 0x7fffffff;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     s.q0[t] = p.single ? (t == 0 ? s.qp * kBlockM : p.n_q) : s.qp * 2 * kBlockM + t * kBlockM;
@@ -206,7 +208,7 @@ __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
     } else {
       n = nkv;
     }
-    s.n_t[t] = n < je ? n : je;
+    s.n_t[t] = kSplit ? (n < je ? n : je) : n;
   }
   s.n_max = s.n_t[0] > s.n_t[1] ? s.n_t[0] : s.n_t[1];
   return s;
@@ -214,6 +216,7 @@ __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
 
 // ------------------------------------------------------------------ roles
 // Runs on the whole producer warp; one elected lane issues the copies.
+template <bool kSplit>
 __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                               const CUtensorMap* tm_q, const CUtensorMap* tm_k,
                               const CUtensorMap* tm_v, uint32_t& ld_count, uint32_t& q_count) {
@@ -221,7 +224,7 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
   const uint32_t q_full = smem_u32(&ctl->q_full), q_empty = smem_u32(&ctl->q_empty);
   uint32_t slot = 0, phase = 0;
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
-    const ItemShape s = decode_item(item, p);
+    const ItemShape s = decode_item<kSplit>(item, p);
     if (s.n_max <= s.jb) continue;  // no key tiles in this item
     if (!mbar_wait_warp(q_empty, (q_count & 1) ^ 1, abort_flag, p.status,
                         kStatusTimeoutProducer, p.limit_ns))
@@ -262,6 +265,7 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
 // descriptors live in uniform registers) and one elected lane issues the
 // tcgen05 instructions.  Per key tile j the issue order is
 //   S_0(j), S_1(j), O_0 += P_0(j-1) V_{j-1}, O_1 += P_1(j-1) V_{j-1}.
+template <bool kSplit>
 __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                          uint32_t tmem) {
   volatile int* abort_flag = &ctl->abort;
@@ -281,7 +285,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
   };
 
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
-    const ItemShape s = decode_item(item, p);
+    const ItemShape s = decode_item<kSplit>(item, p);
     if (s.n_max <= s.jb) continue;  // no key tiles in this item
     if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
     ++q_count;
@@ -371,6 +375,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
   return true;
 }
 
+template <bool kSplit, bool kTurnsAlways>
 __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                              uint32_t tmem, const CUtensorMap* tm_o, int t, int warp_in_group,
                              int lane) {
@@ -387,9 +392,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   const uint32_t o_empty = smem_u32(&ctl->o_empty[t]);
   const uint32_t stage = smem_base + kSmemO + t * kTileBytes;
   const float c = p.scale_log2;
-  const bool leader = (row == 0);
   uint32_t s_cnt = 0, od_cnt = 0, wg_cnt = 0;
-  bool first_item = true;
 
   auto wait = [&](uint32_t bar, uint32_t parity) {
     return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax,
@@ -406,7 +409,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   uint32_t turn_cnt = 0;
   // Turns are taken only in items where both tiles have key tiles; a lone
   // tile runs freely.
-  bool use_turns = true;
+  bool use_turns = true;  // constant in kernels whose items all have two tiles
   auto take_turn = [&]() {
     if (!use_turns) return true;
     return wait(turn_mine, (turn_cnt & 1) ^ (t == 0 ? 1u : 0u));
@@ -501,16 +504,16 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   };
 
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
-    const ItemShape s = decode_item(item, p);
+    const ItemShape s = decode_item<kSplit>(item, p);
     const int n_t = s.n_t[t];
-    use_turns = s.n_t[0] > s.jb && s.n_t[1] > s.jb;
+    use_turns = kTurnsAlways || (s.n_t[0] > s.jb && s.n_t[1] > s.jb);
     if (n_t <= s.jb) {
       for (int j = s.jb; j < s.n_max; ++j) {
         if (!take_turn()) return false;
         pass_turn();
       }
-      if (p.n_split > 1 && s.valid[t]) {
-        if (!split_epilogue(s, nullptr, -INFINITY, 0.f)) return false;
+      if constexpr (kSplit) {
+        if (s.valid[t] && !split_epilogue(s, nullptr, -INFINITY, 0.f)) return false;
       }
       continue;
     }
@@ -650,7 +653,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(o_empty);
-    if (p.n_split > 1) {
+    if constexpr (kSplit) {
       if (!split_epilogue(s, orr, m_used, l)) return false;
       continue;
     }
@@ -661,8 +664,11 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     for (int i = 0; i < 32; ++i)
       h[i] = pack_half2(__uint_as_float(orr[2 * i]) * inv, __uint_as_float(orr[2 * i + 1]) * inv);
 
-    if (leader && !first_item) bulk_wait_group_read0();
-    if (!wg_sync()) return false;
+    // Each warp stores its own 32 rows: a 4 KiB slice of the staging tile
+    // and one TMA store, so the epilogue needs no warpgroup barrier.  The
+    // slice is rewritten only after this warp's previous store has read it.
+    if (lane == 0) bulk_wait_group_read0();
+    __syncwarp();
     const uint32_t row_addr = stage + row * 128;
 #pragma unroll
     for (int ch = 0; ch < 8; ++ch) {
@@ -672,16 +678,21 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
                    : "memory");
     }
     fence_proxy_async_smem();
-    if (!wg_sync()) return false;
-    if (leader) {
-      tma_store_3d(tm_o, stage, 0, s.q0[t], s.bh);
+    __syncwarp();
+    const int warp_row0 = s.q0[t] + warp_in_group * 32;
+    if (lane == 0 && warp_row0 < p.n_q) {
+      tma_store_3d(tm_o, stage + warp_in_group * 32 * 128, 0, warp_row0, s.bh);
       bulk_commit_group();
     }
-    first_item = false;
   }
   return true;
 }
 
+// kSplit: key-range split items (fp32 partials, merged by the last split).
+// kTurnsAlways: every item has two query tiles with key tiles, so the MUFU
+// turns are never skipped.  Separate instantiations keep the split merge and
+// the per-item turn check out of the main path's code.
+template <bool kSplit, bool kTurnsAlways>
 __global__ void __launch_bounds__(kNumThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -733,15 +744,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // Softmax warpgroups take the registers the producer/MMA warpgroup gives
     // up: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
     asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
-    const bool ok = softmax_loop(p, ctl, smem_base, tmem, &tm_o, warp / 4, warp % 4, lane);
+    const bool ok =
+        softmax_loop<kSplit, kTurnsAlways>(p, ctl, smem_base, tmem, &tm_o, warp / 4, warp % 4, lane);
     (void)ok;
-    if (warp % 4 == 0 && lane == 0) bulk_wait_group0();
+    if (lane == 0) bulk_wait_group0();  // this warp's output stores
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
   }
   if (warp == 8) {
     uint32_t ld_count = 0, q_count = 0;
-    const bool ok = producer_loop(p, ctl, smem_base, &tm_q, &tm_k, &tm_v, ld_count, q_count);
+    const bool ok = producer_loop<kSplit>(p, ctl, smem_base, &tm_q, &tm_k, &tm_v, ld_count, q_count);
     if (!ok && lane == 0) {
       // Let every copy this warp started land before the block exits.
       const uint32_t n = ld_count < kKvSlots ? ld_count : kKvSlots;
@@ -756,7 +768,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     __syncwarp();
   } else if (warp == 9) {
-    mma_loop(p, ctl, smem_base, tmem);
+    mma_loop<kSplit>(p, ctl, smem_base, tmem);
     // Every MMA (and the barrier arrivals its commits perform) finishes
     // before tensor memory and shared memory are released.
     if (lane == 0) {
@@ -940,8 +952,13 @@ int ensure_device(int dev, DeviceState** out) {
                        major, minor);
     cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "%s", cudaGetErrorString(e));
-    e = cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(fa::kSmemBytes));
+    for (const void* fn : {reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, true>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<true, false>)}) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(fa::kSmemBytes));
+      if (e != cudaSuccess) break;
+    }
     if (e != cudaSuccess)
       return set_error(FA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     void* sym = nullptr;
@@ -963,10 +980,11 @@ int ensure_device(int dev, DeviceState** out) {
   return FA_OK;
 }
 
-int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t slices) {
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t slices,
+             uint32_t box_rows) {
   const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(slices)};
   const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(rows) * 128};
-  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t box[3] = {64, box_rows, 1};
   const cuuint32_t estride[3] = {1, 1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims,
                         strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1001,10 +1019,11 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   if (rc != FA_OK) return rc;
 
   CUtensorMap tq, tk, tv, to;
-  if ((rc = make_map(&tq, q, n_q, bh)) != FA_OK) return rc;
-  if ((rc = make_map(&tk, k, n_k, bh)) != FA_OK) return rc;
-  if ((rc = make_map(&tv, v, n_k, bh)) != FA_OK) return rc;
-  if ((rc = make_map(&to, o, n_q, bh)) != FA_OK) return rc;
+  // q, k, v: 128-row tiles; o: 32-row slices (one TMA store per softmax warp)
+  if ((rc = make_map(&tq, q, n_q, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tk, k, n_k, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tv, v, n_k, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&to, o, n_q, bh, 32)) != FA_OK) return rc;
 
   fa::FwdParams p;
   p.n_q = static_cast<int>(n_q);
@@ -1062,7 +1081,14 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   p.unit = (p.n_split == 1 && p.n_items > d->sms) ? 2 : 1;
   const int units = (p.n_items + p.unit - 1) / p.unit;
   const int grid = units < d->sms ? units : d->sms;
-  fa::fa_fwd_kernel<<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  if (p.n_split > 1) {
+    fa::fa_fwd_kernel<true, false><<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  } else if (!p.single && sp.n_qtiles % 2 == 0) {
+    // every work item is a pair of query tiles, each with at least one key tile
+    fa::fa_fwd_kernel<false, true><<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  } else {
+    fa::fa_fwd_kernel<false, false><<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   return FA_OK;
