@@ -7,12 +7,14 @@
 //
 //   warp 8      TMA producer: Q tiles of the current work item, then K_j/V_j
 //               tiles through a ring of swizzled shared-memory slots.
-//   warp 9      MMA issuer (one elected lane): S_t = Q_t K_j^T (SS form) and
-//               O_t += P_t V_j (P read straight from tensor memory, TS form).
-//               It also owns the tensor-memory allocation.
+//   warp 10     MMA issuer (one elected lane) for S_t = Q_t K_j^T (SS form).
+//   warp 11     MMA issuer for O_t += P_t V_j (P read straight from tensor
+//               memory, TS form).  Issuing tcgen05.mma slows the softmax
+//               warps of the same SM sub-partition, so the two issue streams
+//               sit on different sub-partitions.
+//   warp 9      owns the tensor-memory allocation, otherwise idle.
 //   warps 0-3   softmax for query tile 0 of the work item, one thread per row.
 //   warps 4-7   softmax for query tile 1 (ping-pong partner of tile 0).
-//   warps 10-11 idle (kept so the block is three whole warpgroups).
 //
 // A work item is one (batch*head, query-pair) unit: 256 query rows as two
 // 128-row tiles (one tile per item for short problems; with a key-range split
@@ -21,7 +23,7 @@
 //   S_t  128 x 128 fp32   (columns   0 / 128)
 //   O_t  128 x  64 fp32   (columns 256 / 320)
 //   P_t  128 x 128 fp16   (columns 384 / 448, two halves per column)
-// so the MMA warp can compute S_t(j+1) while the softmax warps are still
+// so S_t(j+1) can be computed while the softmax warps are still
 // turning S_t(j) into P_t(j).  Each softmax warp writes its 32 rows of the
 // normalised output with its own TMA store.  The two softmax warpgroups take turns on the
 // MUFU (16 ex2/clk/SM, the unit that bounds attention at head dimension 64):
@@ -61,6 +63,12 @@
 #ifndef FA_POLY_PAIRS
 #define FA_POLY_PAIRS 0  // of every 8 exponent pairs, this many use the FMA-pipe polynomial
                          // (0 measured fastest in this kernel on a B200)
+#endif
+#ifndef FA_S_WARP
+#define FA_S_WARP 10  // issues S = Q K^T (and P V when FA_PV_WARP is the same warp; 8 < warp < 12)
+#endif
+#ifndef FA_PV_WARP
+#define FA_PV_WARP 11  // issues O += P V
 #endif
 #ifndef FA_EARLY_PASS
 #define FA_EARLY_PASS 16  // exponent pairs still to do when the MUFU turn is handed over
@@ -121,7 +129,7 @@ struct SharedCtl {
   uint64_t s_full[2], s_empty[2], p_full[2], o_done[2], o_empty[2];
   uint64_t exp_turn[2];  // alternates the two softmax warpgroups' exponential phases
   uint64_t wg_bar[2];    // a tile's four softmax warps (key-range split epilogue)
-  uint64_t drain;
+  uint64_t drain[2];     // one per MMA-issuing warp
   uint32_t tmem_base;
   int abort;
   int merge_flag[2];
@@ -261,11 +269,14 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
   return true;
 }
 
-// Runs on the whole MMA warp: waits and bookkeeping are warp-uniform (so the
+// Runs on a whole MMA warp: waits and bookkeeping are warp-uniform (so the
 // descriptors live in uniform registers) and one elected lane issues the
-// tcgen05 instructions.  Per key tile j the issue order is
-//   S_0(j), S_1(j), O_0 += P_0(j-1) V_{j-1}, O_1 += P_1(j-1) V_{j-1}.
-template <bool kSplit>
+// tcgen05 instructions.  Two warps on different SM sub-partitions share the
+// work (kIssueS: S_t = Q_t K_j^T; kIssuePV: O_t += P_t V_j), because issuing
+// tcgen05.mma slows the softmax warps on the issuing sub-partition.  Per key
+// tile j the order is S_0(j), S_1(j), then O_0 += P_0(j-1) V_{j-1},
+// O_1 += P_1(j-1) V_{j-1}.
+template <bool kSplit, bool kIssueS, bool kIssuePV>
 __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                          uint32_t tmem) {
   volatile int* abort_flag = &ctl->abort;
@@ -287,18 +298,19 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
     const ItemShape s = decode_item<kSplit>(item, p);
     if (s.n_max <= s.jb) continue;  // no key tiles in this item
-    if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
-    ++q_count;
-    tc_fence_after();
+    if (kIssueS) {
+      if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
+      ++q_count;
+      tc_fence_after();
+    }
     uint32_t v_slot = 0, v_phase = 0;  // ring position of V_{j-1}
     const bool trace_on = item == first_item_of_block() && threadIdx.x % 32 == 0;
     (void)trace_on;
     for (int j = s.jb; j <= s.n_max; ++j) {
       TRACE(2, j, 0);
       uint32_t next_v_slot = 0, next_v_phase = 0;
+      const uint32_t ks = slot, kph = phase;  // ring position of K_j
       if (j < s.n_max) {
-        // ---- S_t = Q_t K_j^T for every tile that still needs key tile j
-        const uint32_t ks = slot, kph = phase;
         next_v_slot = ks + 1 == kKvSlots ? 0 : ks + 1;
         next_v_phase = ks + 1 == kKvSlots ? kph ^ 1 : kph;
         slot += 2;  // past K_j and V_j
@@ -306,6 +318,9 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
           slot -= kKvSlots;
           phase ^= 1;
         }
+      }
+      if (kIssueS && j < s.n_max) {
+        // ---- S_t = Q_t K_j^T for every tile that still needs key tile j
         if (!wait(smem_u32(&ctl->kv_full[ks]), kph)) return false;
         TRACE(2, j, 1);
         tc_fence_after();
@@ -333,7 +348,7 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
         }
         __syncwarp();
       }
-      if (j > s.jb) {
+      if (kIssuePV && j > s.jb) {
         // ---- O_t += P_t V_{j-1}
         const int jj = j - 1;
         if (!wait(smem_u32(&ctl->kv_full[v_slot]), v_phase)) return false;
@@ -721,7 +736,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&ctl->exp_turn[t]), 4);
       mbar_init(smem_u32(&ctl->wg_bar[t]), 4);
     }
-    mbar_init(smem_u32(&ctl->drain), 1);
+    mbar_init(smem_u32(&ctl->drain[0]), 1);
+    mbar_init(smem_u32(&ctl->drain[1]), 1);
     ctl->abort = 0;
     fence_mbar_init();
   }
@@ -767,13 +783,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                   kStatusTimeoutDrain, kDrainLimitNs);
     }
     __syncwarp();
-  } else if (warp == 9) {
-    mma_loop<kSplit>(p, ctl, smem_base, tmem);
-    // Every MMA (and the barrier arrivals its commits perform) finishes
-    // before tensor memory and shared memory are released.
+  } else if (warp == FA_S_WARP || warp == FA_PV_WARP) {
+    if (warp == FA_S_WARP)
+      mma_loop<kSplit, true, FA_S_WARP == FA_PV_WARP>(p, ctl, smem_base, tmem);
+    else
+      mma_loop<kSplit, false, true>(p, ctl, smem_base, tmem);
+    // Every MMA this warp issued (and the barrier arrivals its commits
+    // perform) finishes before tensor memory and shared memory are released.
+    const uint32_t drain = smem_u32(&ctl->drain[warp == FA_S_WARP ? 0 : 1]);
     if (lane == 0) {
-      tc_commit(smem_u32(&ctl->drain));
-      mbar_wait(smem_u32(&ctl->drain), 0, nullptr, p.status, kStatusTimeoutDrain, kDrainLimitNs);
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutDrain, kDrainLimitNs);
     }
     __syncwarp();
   }
