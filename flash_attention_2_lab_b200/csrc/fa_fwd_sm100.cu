@@ -64,6 +64,9 @@
 #define FA_POLY_PAIRS 0  // of every 8 exponent pairs, this many use the FMA-pipe polynomial
                          // (0 measured fastest in this kernel on a B200)
 #endif
+#ifndef FA_PRODUCER_WARP
+#define FA_PRODUCER_WARP 8  // TMA producer
+#endif
 #ifndef FA_S_WARP
 #define FA_S_WARP 10  // issues S = Q K^T (and P V when FA_PV_WARP is the same warp; 8 < warp < 12)
 #endif
@@ -741,7 +744,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     ctl->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == FA_PRODUCER_WARP && lane == 0) {
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
@@ -767,7 +770,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
   }
-  if (warp == 8) {
+  if (warp == FA_PRODUCER_WARP) {
     uint32_t ld_count = 0, q_count = 0;
     const bool ok = producer_loop<kSplit>(p, ctl, smem_base, &tm_q, &tm_k, &tm_v, ld_count, q_count);
     if (!ok && lane == 0) {
