@@ -23,12 +23,12 @@
 //   S_t  128 x 128 fp32   (columns   0 / 128)
 //   O_t  128 x  64 fp32   (columns 256 / 320)
 //   P_t  128 x 128 fp16   (columns 384 / 448, two halves per column)
-// so S_t(j+1) can be computed while the softmax warps are still
-// turning S_t(j) into P_t(j).  Each softmax warp writes its 32 rows of the
-// normalised output with its own TMA store.  The two softmax warpgroups take turns on the
-// MUFU (16 ex2/clk/SM, the unit that bounds attention at head dimension 64):
-// one tile's exponentials overlap the other tile's S load, row max and P
-// store.
+// so S_t(j+1) can be computed while the softmax warps are still turning
+// S_t(j) into P_t(j).  Each softmax warp writes its 32 rows of the normalised
+// output with its own TMA store.  The two softmax warpgroups take turns on
+// the MUFU (16 ex2/clk/SM, the unit that bounds attention at head dimension
+// 64): one tile's exponentials overlap the other tile's S load, row max and
+// P store.
 //
 // Online softmax follows the reference's tile update
 // (csrc/tensorcore_attention.cu:448-671): running row max m, running sum l,
@@ -64,15 +64,22 @@
 #define FA_POLY_PAIRS 0  // of every 8 exponent pairs, this many use the FMA-pipe polynomial
                          // (0 measured fastest in this kernel on a B200)
 #endif
+// Roles of the third warpgroup (warps 8-11): the producer and the MMA issuers
+// must be different warps of that group, except that one warp may issue both
+// kinds of MMA (FA_S_WARP == FA_PV_WARP).
 #ifndef FA_PRODUCER_WARP
 #define FA_PRODUCER_WARP 8  // TMA producer
 #endif
 #ifndef FA_S_WARP
-#define FA_S_WARP 10  // issues S = Q K^T (and P V when FA_PV_WARP is the same warp; 8 < warp < 12)
+#define FA_S_WARP 10  // issues S = Q K^T
 #endif
 #ifndef FA_PV_WARP
 #define FA_PV_WARP 11  // issues O += P V
 #endif
+static_assert(FA_PRODUCER_WARP >= 8 && FA_PRODUCER_WARP <= 11 && FA_S_WARP >= 8 &&
+                  FA_S_WARP <= 11 && FA_PV_WARP >= 8 && FA_PV_WARP <= 11 &&
+                  FA_PRODUCER_WARP != FA_S_WARP && FA_PRODUCER_WARP != FA_PV_WARP,
+              "producer and MMA issuers must be distinct warps of warps 8-11");
 #ifndef FA_EARLY_PASS
 #define FA_EARLY_PASS 16  // exponent pairs still to do when the MUFU turn is handed over
 #endif
