@@ -90,6 +90,23 @@ def test_different_query_key_lengths(nq, nk, causal):
     assert_parity(out, oracle_of(q, k, v, causal), what=f"nq={nq} nk={nk}")
 
 
+# Shapes that select each compiled variant of the kernel on a 148-SM B200 (the
+# host picks the variant; the comments say which path each shape takes):
+#   every work item a pair of query tiles (even tile count, > 74 items);
+#   pairs whose last item has one tile (odd tile count), turns checked per item;
+#   one 128-row tile per item (few items), no MUFU turns;
+#   pairs with a ragged last tile and a key length that is not a tile multiple.
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize(("b", "h", "nq", "nk"), [(2, 40, 1024, 1024), (2, 40, 640, 640),
+                                                  (1, 8, 1024, 1024), (3, 30, 700, 900)])
+def test_kernel_variants_match_fp32(b, h, nq, nk, causal):
+    q, k, v = seeded(b, h, nq, nk, seed=b * 100 + nq)
+    out = abi_forward(q, k, v, causal)
+    torch.cuda.synchronize()
+    assert_parity(out, torch_fp32_reference(q, k, v, causal),
+                  what=f"B{b} H{h} nq={nq} nk={nk} causal={causal}")
+
+
 def test_custom_scale():
     q, k, v = seeded(1, 2, 384, seed=3)
     out = abi_forward(q, k, v, False, scale=0.3)
