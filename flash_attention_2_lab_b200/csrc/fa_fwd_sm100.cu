@@ -80,6 +80,12 @@ static_assert(FA_PRODUCER_WARP >= 8 && FA_PRODUCER_WARP <= 11 && FA_S_WARP >= 8 
                   FA_S_WARP <= 11 && FA_PV_WARP >= 8 && FA_PV_WARP <= 11 &&
                   FA_PRODUCER_WARP != FA_S_WARP && FA_PRODUCER_WARP != FA_PV_WARP,
               "producer and MMA issuers must be distinct warps of warps 8-11");
+#ifndef FA_HALVES
+#define FA_HALVES 1  // short problems: split each query tile's keys between the warpgroups
+#endif
+#ifndef FA_SPLIT_MIN_TILES
+#define FA_SPLIT_MIN_TILES 8  // fewest key tiles per split of the key-range split mode
+#endif
 #ifndef FA_EARLY_PASS
 #define FA_EARLY_PASS 16  // exponent pairs still to do when the MUFU turn is handed over
 #endif
@@ -190,7 +196,7 @@ __device__ __forceinline__ int next_item_of(int item, int unit) {
 }
 #define next_item(item) next_item_of(item, p.unit)
 
-template <bool kSplit>
+template <bool kSplit, bool kHalves = false>
 __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
   ItemShape s;
   int k;
@@ -228,13 +234,30 @@ __device__ __forceinline__ ItemShape decode_item(int item, const FwdParams& p) {
     }
     s.n_t[t] = kSplit ? (n < je ? n : je) : n;
   }
+  if constexpr (kHalves) {
+    // One query tile (p.single); its key tiles are split between the two
+    // softmax warpgroups: tile slot 0 takes key tiles [0, n_t[0]), tile slot
+    // 1 the rest, [n_t[0], n_t[0] + n_t[1]), against the same query rows.
+    const int full = s.n_t[0];
+    s.q0[1] = s.q0[0];
+    s.valid[1] = false;  // only tile slot 0 writes output
+    s.n_t[0] = (full + 1) / 2;
+    s.n_t[1] = full - s.n_t[0];
+  }
   s.n_max = s.n_t[0] > s.n_t[1] ? s.n_t[0] : s.n_t[1];
   return s;
 }
 
+// First key tile of tile slot t (non-zero only for the second half of a
+// split key range).
+template <bool kHalves>
+__device__ __forceinline__ int key_offset(const ItemShape& s, int t) {
+  return (kHalves && t == 1) ? s.n_t[0] : 0;
+}
+
 // ------------------------------------------------------------------ roles
 // Runs on the whole producer warp; one elected lane issues the copies.
-template <bool kSplit>
+template <bool kSplit, bool kHalves>
 __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                               const CUtensorMap* tm_q, const CUtensorMap* tm_k,
                               const CUtensorMap* tm_v, uint32_t& ld_count, uint32_t& q_count) {
@@ -242,12 +265,12 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
   const uint32_t q_full = smem_u32(&ctl->q_full), q_empty = smem_u32(&ctl->q_empty);
   uint32_t slot = 0, phase = 0;
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
-    const ItemShape s = decode_item<kSplit>(item, p);
+    const ItemShape s = decode_item<kSplit, kHalves>(item, p);
     if (s.n_max <= s.jb) continue;  // no key tiles in this item
     if (!mbar_wait_warp(q_empty, (q_count & 1) ^ 1, abort_flag, p.status,
                         kStatusTimeoutProducer, p.limit_ns))
       return false;
-    const uint32_t nq = (s.n_t[1] > s.jb) ? 2 : 1;
+    const uint32_t nq = (!kHalves && s.n_t[1] > s.jb) ? 2 : 1;
     if (elect_one()) {
       mbar_arrive_expect_tx(q_full, nq * kTileBytes);
       tma_load_3d(smem_base + kSmemQ, tm_q, q_full, 0, s.q0[0], s.bh);
@@ -256,22 +279,29 @@ __device__ bool producer_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_
     __syncwarp();
     ++q_count;
     for (int j = s.jb; j < s.n_max; ++j) {
+      // One K/V pair per step, or with a split key range one per active half
+      // (the half's K then V), in the order the MMA warps walk the ring.
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        if (!mbar_wait_warp(smem_u32(&ctl->kv_empty[slot]), phase ^ 1, abort_flag, p.status,
-                            kStatusTimeoutProducer, p.limit_ns))
-          return false;
-        if (elect_one()) {
-          const uint32_t full = smem_u32(&ctl->kv_full[slot]);
-          mbar_arrive_expect_tx(full, kTileBytes);
-          tma_load_3d(smem_base + kSmemKV + slot * kTileBytes, which ? tm_v : tm_k, full, 0,
-                      j * kBlockN, s.bh);
-        }
-        __syncwarp();
-        ++ld_count;
-        if (++slot == kKvSlots) {
-          slot = 0;
-          phase ^= 1;
+      for (int g = 0; g < (kHalves ? 2 : 1); ++g) {
+        if (kHalves && j >= s.n_t[g]) continue;
+        const int kt = key_offset<kHalves>(s, g) + j;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          if (!mbar_wait_warp(smem_u32(&ctl->kv_empty[slot]), phase ^ 1, abort_flag, p.status,
+                              kStatusTimeoutProducer, p.limit_ns))
+            return false;
+          if (elect_one()) {
+            const uint32_t full = smem_u32(&ctl->kv_full[slot]);
+            mbar_arrive_expect_tx(full, kTileBytes);
+            tma_load_3d(smem_base + kSmemKV + slot * kTileBytes, which ? tm_v : tm_k, full, 0,
+                        kt * kBlockN, s.bh);
+          }
+          __syncwarp();
+          ++ld_count;
+          if (++slot == kKvSlots) {
+            slot = 0;
+            phase ^= 1;
+          }
         }
       }
     }
@@ -400,7 +430,110 @@ __device__ bool mma_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
   return true;
 }
 
-template <bool kSplit, bool kTurnsAlways>
+// MMA issue for items whose single query tile has its key range split
+// between the two tile slots (short problems): slot t computes
+// S_t = Q K_{o_t + j}^T and O_t += P_t V_{o_t + j} with o_0 = 0 and
+// o_1 = n_t[0], both against the one Q tile.  Per step the ring holds K, V of
+// slot 0 and then K, V of slot 1 (when active), as the producer loads them.
+template <bool kIssueS, bool kIssuePV>
+__device__ bool mma_loop_halves(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
+                                uint32_t tmem) {
+  volatile int* abort_flag = &ctl->abort;
+  constexpr uint32_t idesc_qk = idesc_f16_f32(kBlockM, kBlockN, false);
+  constexpr uint32_t idesc_pv = idesc_f16_f32(kBlockM, kHeadDim, true);
+  uint32_t slot = 0, phase = 0;
+  uint32_t q_count = 0;
+  uint32_t s_cnt[2] = {0, 0}, p_cnt[2] = {0, 0}, o_cnt[2] = {0, 0};
+  const uint64_t dq = smem_desc_sw128(smem_base + kSmemQ, 16, 1024);
+  const uint64_t dkv = smem_desc_sw128(smem_base + kSmemKV, 16, 1024);
+  constexpr uint64_t kTileDesc = kTileBytes >> 4;
+
+  auto wait = [&](uint32_t bar, uint32_t parity) {
+    return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutMma, p.limit_ns);
+  };
+
+  for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
+    const ItemShape s = decode_item<false, true>(item, p);
+    if (s.n_max <= 0) continue;
+    if (kIssueS) {
+      if (!wait(smem_u32(&ctl->q_full), q_count & 1)) return false;
+      ++q_count;
+      tc_fence_after();
+    }
+    uint32_t v_slot[2] = {0, 0}, v_phase[2] = {0, 0};  // ring position of V of the last step
+    for (int j = 0; j <= s.n_max; ++j) {
+      uint32_t nv_slot[2] = {0, 0}, nv_phase[2] = {0, 0};
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (j >= s.n_t[t]) continue;
+        const uint32_t ks = slot, kph = phase;
+        nv_slot[t] = ks + 1 == kKvSlots ? 0 : ks + 1;
+        nv_phase[t] = ks + 1 == kKvSlots ? kph ^ 1 : kph;
+        slot += 2;  // past this slot's K and V
+        if (slot >= kKvSlots) {
+          slot -= kKvSlots;
+          phase ^= 1;
+        }
+        if (kIssueS) {
+          // ---- S_t = Q K_{o_t + j}^T
+          if (!wait(smem_u32(&ctl->kv_full[ks]), kph)) return false;
+          if (!wait(smem_u32(&ctl->s_empty[t]), (s_cnt[t] & 1) ^ 1)) return false;
+          ++s_cnt[t];
+          tc_fence_after();
+          if (elect_one()) {
+            const uint64_t dk = dkv + ks * kTileDesc;
+#pragma unroll
+            for (int kk = 0; kk < kHeadDim / 16; ++kk)
+              mma_ss_f16(tmem + col_s(t), dq + 2 * kk, dk + 2 * kk, idesc_qk, kk > 0);
+            tc_commit(smem_u32(&ctl->s_full[t]));
+            tc_commit(smem_u32(&ctl->kv_empty[ks]));
+          }
+          __syncwarp();
+        }
+      }
+      if (kIssueS && j == s.n_max - 1) {
+        if (elect_one()) tc_commit(smem_u32(&ctl->q_empty));
+        __syncwarp();
+      }
+      if (kIssuePV && j > 0) {
+        // ---- O_t += P_t V_{o_t + j - 1}
+        const int jj = j - 1;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (jj >= s.n_t[t]) continue;
+          if (!wait(smem_u32(&ctl->kv_full[v_slot[t]]), v_phase[t])) return false;
+          if (jj == 0) {
+            // O_t is overwritten by this item's first PV: the previous item's
+            // epilogue must have read it.
+            if (!wait(smem_u32(&ctl->o_empty[t]), (o_cnt[t] & 1) ^ 1)) return false;
+            ++o_cnt[t];
+          }
+          if (!wait(smem_u32(&ctl->p_full[t]), p_cnt[t] & 1)) return false;
+          ++p_cnt[t];
+          tc_fence_after();
+          if (elect_one()) {
+            const uint64_t dv = dkv + v_slot[t] * kTileDesc;
+#pragma unroll
+            for (int kk = 0; kk < kBlockN / 16; ++kk)
+              mma_ts_f16(tmem + col_o(t), tmem + col_p(t) + kk * 8, dv + 128 * kk, idesc_pv,
+                         (jj > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(smem_u32(&ctl->o_done[t]));
+            tc_commit(smem_u32(&ctl->kv_empty[v_slot[t]]));
+          }
+          __syncwarp();
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        v_slot[t] = nv_slot[t];
+        v_phase[t] = nv_phase[t];
+      }
+    }
+  }
+  return true;
+}
+
+template <bool kSplit, bool kTurnsAlways, bool kHalves>
 __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                              uint32_t tmem, const CUtensorMap* tm_o, int t, int warp_in_group,
                              int lane) {
@@ -418,6 +551,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   const uint32_t stage = smem_base + kSmemO + t * kTileBytes;
   const float c = p.scale_log2;
   uint32_t s_cnt = 0, od_cnt = 0, wg_cnt = 0;
+  uint32_t merge_cnt = 0;  // items merged (split key range within the block)
 
   auto wait = [&](uint32_t bar, uint32_t parity) {
     return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax,
@@ -529,10 +663,10 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
   };
 
   for (int item = first_item_of_block(); item < p.n_items; item = next_item(item)) {
-    const ItemShape s = decode_item<kSplit>(item, p);
+    const ItemShape s = decode_item<kSplit, kHalves>(item, p);
     const int n_t = s.n_t[t];
     use_turns = kTurnsAlways || (s.n_t[0] > s.jb && s.n_t[1] > s.jb);
-    if (n_t <= s.jb) {
+    if (!kHalves && n_t <= s.jb) {
       for (int j = s.jb; j < s.n_max; ++j) {
         if (!take_turn()) return false;
         pass_turn();
@@ -563,7 +697,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty);
 
-      const int kv0 = j * kBlockN;
+      const int kv0 = (key_offset<kHalves>(s, t) + j) * kBlockN;
       const bool need_mask =
           (p.causal && kv0 + kBlockN - 1 > s.q0[t]) || (kv0 + kBlockN > p.n_k);
       if (need_mask) {
@@ -668,16 +802,71 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     }
 
     // ---- epilogue: O / l -> fp16 -> swizzled staging tile -> TMA store
-    if (!wait(o_done, od_cnt & 1)) return false;
-    ++od_cnt;
-    tc_fence_after();
+    if (!kHalves || n_t > 0) {
+      if (!wait(o_done, od_cnt & 1)) return false;  // the last P V of this tile slot
+      ++od_cnt;
+    }
     uint32_t orr[64];
-    tmem_ld32(t_o, orr);
-    tmem_ld32(t_o + 32, orr + 32);
-    tc_wait_ld();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(o_empty);
+    if constexpr (kHalves) {
+      // The two tile slots hold the same query rows over two halves of the
+      // key range.  Slot 1 hands its (max used, sum) to slot 0 through
+      // shared memory (the unused output staging tile of slot 1); slot 0
+      // reads both partial numerators from tensor memory and merges:
+      // m = max(m0, m1), O = O0 2^((m0-m)c) + O1 2^((m1-m)c), likewise l.
+      float* ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) - kSmemCtl + kSmemO +
+                                           kTileBytes);
+      const uint32_t ml_free = smem_u32(&ctl->wg_bar[0]);   // slot 0 has read (m, l)
+      const uint32_t ml_ready = smem_u32(&ctl->wg_bar[1]);  // slot 1 has written them
+      if (t == 1) {
+        if (!wait(ml_free, (merge_cnt & 1) ^ 1)) return false;
+        ++merge_cnt;
+        ml[row] = n_t > 0 ? m_used : -INFINITY;
+        ml[kBlockM + row] = n_t > 0 ? l : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ml_ready);
+        continue;
+      }
+      if (!wait(ml_ready, merge_cnt & 1)) return false;
+      ++merge_cnt;
+      tc_fence_after();
+      const float m1 = ml[row], l1 = ml[kBlockM + row];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ml_free);
+      tmem_ld32(t_o, orr);
+      tmem_ld32(t_o + 32, orr + 32);
+      tc_wait_ld();
+      const bool other = s.n_t[1] > 0;
+      if (other) {
+        const float m = fmaxf(m_used, m1);
+        const float w0 = ex2_approx((m_used - m) * c), w1 = ex2_approx((m1 - m) * c);
+        l = l * w0 + l1 * w1;
+        const uint32_t t_o1 = tmem + lane_base + col_o(1);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t o1[32];
+          tmem_ld32(t_o1 + 32 * h, o1);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            orr[32 * h + i] = __float_as_uint(
+                fmaf(__uint_as_float(orr[32 * h + i]), w0, __uint_as_float(o1[i]) * w1));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(o_empty);
+        if (other) mbar_arrive(smem_u32(&ctl->o_empty[1]));
+      }
+    } else {
+      tc_fence_after();
+      tmem_ld32(t_o, orr);
+      tmem_ld32(t_o + 32, orr + 32);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_empty);
+    }
     if constexpr (kSplit) {
       if (!split_epilogue(s, orr, m_used, l)) return false;
       continue;
@@ -715,9 +904,11 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
 
 // kSplit: key-range split items (fp32 partials, merged by the last split).
 // kTurnsAlways: every item has two query tiles with key tiles, so the MUFU
-// turns are never skipped.  Separate instantiations keep the split merge and
-// the per-item turn check out of the main path's code.
-template <bool kSplit, bool kTurnsAlways>
+// turns are never skipped.  kHalves: one query tile per item whose key range
+// is split between the two softmax warpgroups and merged in the block (short
+// problems).  Separate instantiations keep the split merge and the per-item
+// turn check out of the main path's code.
+template <bool kSplit, bool kTurnsAlways, bool kHalves>
 __global__ void __launch_bounds__(kNumThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -771,7 +962,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // up: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
     asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     const bool ok =
-        softmax_loop<kSplit, kTurnsAlways>(p, ctl, smem_base, tmem, &tm_o, warp / 4, warp % 4, lane);
+        softmax_loop<kSplit, kTurnsAlways, kHalves>(p, ctl, smem_base, tmem, &tm_o, warp / 4,
+                                                    warp % 4, lane);
     (void)ok;
     if (lane == 0) bulk_wait_group0();  // this warp's output stores
   } else {
@@ -779,7 +971,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   }
   if (warp == FA_PRODUCER_WARP) {
     uint32_t ld_count = 0, q_count = 0;
-    const bool ok = producer_loop<kSplit>(p, ctl, smem_base, &tm_q, &tm_k, &tm_v, ld_count, q_count);
+    const bool ok = producer_loop<kSplit, kHalves>(p, ctl, smem_base, &tm_q, &tm_k, &tm_v,
+                                                   ld_count, q_count);
     if (!ok && lane == 0) {
       // Let every copy this warp started land before the block exits.
       const uint32_t n = ld_count < kKvSlots ? ld_count : kKvSlots;
@@ -794,10 +987,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     __syncwarp();
   } else if (warp == FA_S_WARP || warp == FA_PV_WARP) {
-    if (warp == FA_S_WARP)
-      mma_loop<kSplit, true, FA_S_WARP == FA_PV_WARP>(p, ctl, smem_base, tmem);
-    else
-      mma_loop<kSplit, false, true>(p, ctl, smem_base, tmem);
+    if (warp == FA_S_WARP) {
+      if constexpr (kHalves)
+        mma_loop_halves<true, FA_S_WARP == FA_PV_WARP>(p, ctl, smem_base, tmem);
+      else
+        mma_loop<kSplit, true, FA_S_WARP == FA_PV_WARP>(p, ctl, smem_base, tmem);
+    } else {
+      if constexpr (kHalves)
+        mma_loop_halves<false, true>(p, ctl, smem_base, tmem);
+      else
+        mma_loop<kSplit, false, true>(p, ctl, smem_base, tmem);
+    }
     // Every MMA this warp issued (and the barrier arrivals its commits
     // perform) finishes before tensor memory and shared memory are released.
     const uint32_t drain = smem_u32(&ctl->drain[warp == FA_S_WARP ? 0 : 1]);
@@ -912,7 +1112,7 @@ SplitPlan plan_split(int64_t bh, int64_t n_q, int64_t n_k, int sms) {
   // no split on a B200.
   if (g_max_splits != 1 && pairs < sms) {
     int64_t want = sms / pairs;
-    const int64_t cap = nkv / 8;
+    const int64_t cap = nkv / FA_SPLIT_MIN_TILES;
     if (want > cap) want = cap;
     if (g_max_splits > 1 && want > g_max_splits) want = g_max_splits;
     if (want >= 2) {
@@ -982,9 +1182,10 @@ int ensure_device(int dev, DeviceState** out) {
                        major, minor);
     cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "%s", cudaGetErrorString(e));
-    for (const void* fn : {reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, true>),
-                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false>),
-                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<true, false>)}) {
+    for (const void* fn : {reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, true, false>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false, false>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<true, false, false>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false, true>)}) {
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(fa::kSmemBytes));
       if (e != cudaSuccess) break;
@@ -1111,13 +1312,18 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   p.unit = (p.n_split == 1 && p.n_items > d->sms) ? 2 : 1;
   const int units = (p.n_items + p.unit - 1) / p.unit;
   const int grid = units < d->sms ? units : d->sms;
+  constexpr int kThr = fa::kNumThreads;
+  constexpr uint32_t kSm = fa::kSmemBytes;
   if (p.n_split > 1) {
-    fa::fa_fwd_kernel<true, false><<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+    fa::fa_fwd_kernel<true, false, false><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
+  } else if (p.single && FA_HALVES) {
+    // one query tile per block, its key range shared by both softmax warpgroups
+    fa::fa_fwd_kernel<false, false, true><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
   } else if (!p.single && sp.n_qtiles % 2 == 0) {
     // every work item is a pair of query tiles, each with at least one key tile
-    fa::fa_fwd_kernel<false, true><<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+    fa::fa_fwd_kernel<false, true, false><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
   } else {
-    fa::fa_fwd_kernel<false, false><<<grid, fa::kNumThreads, fa::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+    fa::fa_fwd_kernel<false, false, false><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
