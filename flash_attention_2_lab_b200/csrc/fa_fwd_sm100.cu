@@ -1211,8 +1211,28 @@ int ensure_device(int dev, DeviceState** out) {
   return FA_OK;
 }
 
+// cuTensorMapEncodeTiled is a pure function of its arguments, so a small
+// per-thread cache of recent maps is always valid; it saves the encoding when
+// a caller reuses its buffers (a serving or benchmark loop), which matters for
+// short problems whose kernel takes a few microseconds.
+struct MapCacheEntry {
+  CUtensorMap map;
+  const void* ptr = nullptr;
+  int64_t rows = -1, slices = -1;
+  uint32_t box_rows = 0;
+};
+constexpr int kMapCacheSize = 8;
+thread_local MapCacheEntry t_map_cache[kMapCacheSize];
+thread_local int t_map_next = 0;
+
 int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t slices,
              uint32_t box_rows) {
+  for (const MapCacheEntry& e : t_map_cache) {
+    if (e.ptr == ptr && e.rows == rows && e.slices == slices && e.box_rows == box_rows) {
+      *map = e.map;
+      return FA_OK;
+    }
+  }
   const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(slices)};
   const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(rows) * 128};
   const cuuint32_t box[3] = {64, box_rows, 1};
@@ -1222,6 +1242,13 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t slices,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  MapCacheEntry& slot = t_map_cache[t_map_next];
+  t_map_next = (t_map_next + 1) % kMapCacheSize;
+  slot.map = *map;
+  slot.ptr = ptr;
+  slot.rows = rows;
+  slot.slices = slices;
+  slot.box_rows = box_rows;
   return FA_OK;
 }
 
