@@ -1110,7 +1110,13 @@ SplitPlan plan_split(int64_t bh, int64_t n_q, int64_t n_k, int sms) {
   // per split: a block's fixed cost (Q load, pipeline fill, partial write and
   // merge) is worth a few key tiles, so shorter splits measured slower than
   // no split on a B200.
-  if (g_max_splits != 1 && pairs < sms) {
+  // Automatic policy: query tiles that fit in one wave go to one block each,
+  // with the key range split between the block's two softmax warpgroups and
+  // merged in the block (no scratch); measured faster than splitting across
+  // blocks for every such shape on a B200.  An explicit split limit (> 1)
+  // still selects the cross-block split.
+  const bool one_wave_halves = FA_HALVES && g_max_splits == 0 && bh * sp.n_qtiles <= sms;
+  if (g_max_splits != 1 && pairs < sms && !one_wave_halves) {
     int64_t want = sms / pairs;
     const int64_t cap = nkv / FA_SPLIT_MIN_TILES;
     if (want > cap) want = cap;
@@ -1327,11 +1333,11 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
     p.n_items *= sp.n_split;
   }
 
-  // Short problems: when the query pairs would fill at most half the SMs,
-  // make every 128-row query tile its own work item (twice the blocks; a
-  // block's second tile only adds serial work there).
+  // Short problems: when the query tiles fit in one wave, make every 128-row
+  // query tile its own work item (twice the blocks of the pair items; with
+  // FA_HALVES the tile's key range is split between the two warpgroups).
   p.single = 0;
-  if (p.n_split == 1 && 2 * static_cast<int64_t>(p.n_items) <= d->sms) {
+  if (p.n_split == 1 && static_cast<int64_t>(bh) * sp.n_qtiles <= d->sms) {
     p.single = 1;
     p.n_qpairs = sp.n_qtiles;
     p.n_items = static_cast<int>(bh * sp.n_qtiles);

@@ -101,11 +101,16 @@ int fa_selftest_wait_timeout(unsigned long long limit_ns, void* cuda_stream);
 int fa_smem_bytes(void);
 
 /*
- * Key-range split policy for problems with fewer query pairs than SMs:
- * 0 = automatic (default), 1 = never split, k > 1 = at most k splits. In split
- * mode each split writes an fp32 partial result to a scratch buffer and the
- * last split to finish a query tile merges them; the scratch is one buffer per
- * (device, stream), allocated on first need and kept for reuse.
+ * Policy for splitting the key range across blocks (problems with fewer query
+ * pairs than SMs): 0 = automatic (default), 1 = never, k > 1 = into at most k
+ * splits. In split mode each split writes an fp32 partial result to a scratch
+ * buffer and the last split to finish a query tile merges them; the scratch is
+ * one buffer per (device, stream), allocated on first need and kept for reuse.
+ * The automatic policy does not split across blocks when the query tiles fit
+ * in one wave: each tile then gets its own block, whose two softmax
+ * warpgroups take one half of the key range each and merge in the block (no
+ * scratch), which measured faster on a B200; k > 1 selects the cross-block
+ * split for those problems too.
  * No counterpart in the reference (its grid never splits the key range).
  */
 void fa_set_max_splits(int max_splits);

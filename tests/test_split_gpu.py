@@ -14,8 +14,10 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(autouse=True)
-def _auto_split():
-    _native.lib().fa_set_max_splits(0)
+def _split_across_blocks():
+    # An explicit limit selects the cross-block split; the automatic policy
+    # keeps one-wave problems in one block per query tile instead.
+    _native.lib().fa_set_max_splits(16)
     yield
     _native.lib().fa_set_max_splits(0)
     assert read_status() == 0
@@ -45,6 +47,10 @@ def test_split_matches_oracle_and_unsplit(b, h, nq, nk, causal):
     torch.cuda.synchronize()
     assert_parity(whole, ref, what="unsplit")
     assert (split.float() - whole.float()).abs().max().item() < 4e-3
+    _native.lib().fa_set_max_splits(0)
+    auto = abi_forward(q, k, v, causal)
+    torch.cuda.synchronize()
+    assert_parity(auto, ref, what="automatic (in-block key halves)")
 
 
 def test_split_repeated_calls_and_sizes():
