@@ -50,7 +50,9 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <utility>
 
@@ -1046,7 +1048,10 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 namespace {
 
 thread_local char g_last_error[512] = "";
-unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s
+// Process-wide policy, set by fa_set_wait_limit_ns / fa_set_max_splits from
+// any thread and read by every launch.
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;  // 2 s
+std::atomic<unsigned long long> g_wait_limit_ns{kDefaultWaitLimitNs};
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -1071,17 +1076,21 @@ struct DeviceState {
 DeviceState g_dev[kMaxDevices];
 EncodeTiledFn g_encode = nullptr;
 std::mutex g_mutex;
-int g_max_splits = 0;  // 0: automatic, 1: never split the key range, k: at most k splits
+std::atomic<int> g_max_splits{0};  // 0: automatic, 1: never split the key range, k: at most k splits
 
 // Scratch of the key-range split mode, one buffer per (device, stream) so
 // launches on different streams never share it; launches on one stream are
 // ordered.  Allocated on first need, grown when a larger problem arrives, and
-// held until fa_release_workspaces().
+// held until fa_release_workspaces() (also for streams destroyed since).  The
+// map is guarded by g_mutex only while an entry is looked up; the device calls
+// that grow a buffer hold that entry's own mutex, so one stream's allocation
+// never blocks another stream's launch.
 struct Workspace {
+  std::mutex mu;
   void* ptr = nullptr;
   size_t bytes = 0;
 };
-std::map<std::pair<int, cudaStream_t>, Workspace> g_workspaces;
+std::map<std::pair<int, cudaStream_t>, std::unique_ptr<Workspace>> g_workspaces;
 
 // How a launch splits the key range, and the scratch that needs.
 struct SplitPlan {
@@ -1101,6 +1110,7 @@ constexpr size_t kCounterBytes = kMaxSplitTiles * sizeof(int);
 
 SplitPlan plan_split(int64_t bh, int64_t n_q, int64_t n_k, int sms) {
   SplitPlan sp;
+  const int max_splits = g_max_splits.load(std::memory_order_relaxed);
   const int64_t n_qpairs = ((n_q + 127) / 128 + 1) / 2;
   const int64_t pairs = bh * n_qpairs;
   const int64_t nkv = (n_k + 127) / 128;
@@ -1115,12 +1125,12 @@ SplitPlan plan_split(int64_t bh, int64_t n_q, int64_t n_k, int sms) {
   // merged in the block (no scratch); measured faster than splitting across
   // blocks for every such shape on a B200.  An explicit split limit (> 1)
   // still selects the cross-block split.
-  const bool one_wave_halves = FA_HALVES && g_max_splits == 0 && bh * sp.n_qtiles <= sms;
-  if (g_max_splits != 1 && pairs < sms && !one_wave_halves) {
+  const bool one_wave_halves = FA_HALVES && max_splits == 0 && bh * sp.n_qtiles <= sms;
+  if (max_splits != 1 && pairs < sms && !one_wave_halves) {
     int64_t want = sms / pairs;
     const int64_t cap = nkv / FA_SPLIT_MIN_TILES;
     if (want > cap) want = cap;
-    if (g_max_splits > 1 && want > g_max_splits) want = g_max_splits;
+    if (max_splits > 1 && want > max_splits) want = max_splits;
     if (want >= 2) {
       sp.kv_chunk = static_cast<int>((nkv + want - 1) / want);
       sp.n_split = static_cast<int>((nkv + sp.kv_chunk - 1) / sp.kv_chunk);
@@ -1140,29 +1150,32 @@ SplitPlan plan_split(int64_t bh, int64_t n_q, int64_t n_k, int sms) {
 }
 
 int get_workspace(int dev, cudaStream_t stream, size_t need, void** out) {
-  std::lock_guard<std::mutex> lock(g_mutex);
-  Workspace& w = g_workspaces[std::make_pair(dev, stream)];
-  if (w.bytes < need) {
+  Workspace* w = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    std::unique_ptr<Workspace>& slot = g_workspaces[std::make_pair(dev, stream)];
+    if (!slot) slot.reset(new Workspace());
+    w = slot.get();
+  }
+  std::lock_guard<std::mutex> lock(w->mu);
+  if (w->bytes < need) {
     cudaError_t e = cudaSuccess;
-    if (w.ptr != nullptr) {
+    if (w->ptr != nullptr) {
       e = cudaStreamSynchronize(stream);
-      if (e == cudaSuccess) e = cudaFree(w.ptr);
-      w.ptr = nullptr;
-      w.bytes = 0;
+      if (e == cudaSuccess) e = cudaFree(w->ptr);
+      w->ptr = nullptr;
+      w->bytes = 0;
       if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "workspace release: %s", cudaGetErrorString(e));
     }
-    e = cudaMalloc(&w.ptr, need);
+    e = cudaMalloc(&w->ptr, need);
     if (e != cudaSuccess) {
-      w.ptr = nullptr;
+      w->ptr = nullptr;
       return set_error(FA_ERR_CUDA, "workspace allocation (%zu bytes): %s", need,
                        cudaGetErrorString(e));
     }
-    w.bytes = need;
-    // the split counters must start at zero; the kernel leaves them at zero
-    e = cudaMemsetAsync(w.ptr, 0, need, stream);
-    if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "workspace clear: %s", cudaGetErrorString(e));
+    w->bytes = need;
   }
-  *out = w.ptr;
+  *out = w->ptr;
   return FA_OK;
 }
 
@@ -1298,7 +1311,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   p.n_qpairs = static_cast<int>(n_qpairs);
   p.n_items = static_cast<int>(bh * n_qpairs);
   p.status = d->status;
-  p.limit_ns = g_wait_limit_ns;
+  p.limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
   p.dbg = dbg;
 
   p.out = static_cast<__half*>(o);
@@ -1318,14 +1331,14 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
                          "at most %zu",
                          sp.total(), static_cast<size_t>(fa::kNoAllocScratchBytes));
       ws = d->noalloc_scratch;
-      // the split counters must start at zero (a call that timed out could
-      // have left some set); clearing is not an allocation
-      e = cudaMemsetAsync(ws, 0, sp.counters_bytes, stream);
-      if (e != cudaSuccess)
-        return set_error(FA_ERR_CUDA, "scratch clear: %s", cudaGetErrorString(e));
     } else if ((rc = get_workspace(dev, stream, sp.total(), &ws)) != FA_OK) {
       return rc;
     }
+    // The split counters must start at zero.  A completed launch leaves them
+    // at zero, but one whose waits timed out can leave some set, so they are
+    // cleared before every split launch (4 KiB, ordered on the stream).
+    e = cudaMemsetAsync(ws, 0, sp.counters_bytes, stream);
+    if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "scratch clear: %s", cudaGetErrorString(e));
     uint8_t* base = static_cast<uint8_t*>(ws);
     p.counters = reinterpret_cast<int*>(base);
     p.part_ml = reinterpret_cast<float2*>(base + sp.counters_bytes);
@@ -1421,7 +1434,7 @@ int fa_read_status(void* cuda_stream, unsigned int* status_out, int clear) {
 }
 
 void fa_set_wait_limit_ns(unsigned long long limit_ns) {
-  g_wait_limit_ns = limit_ns == 0 ? 2000000000ull : limit_ns;
+  g_wait_limit_ns.store(limit_ns == 0 ? kDefaultWaitLimitNs : limit_ns, std::memory_order_relaxed);
 }
 
 int fa_selftest_wait_timeout(unsigned long long limit_ns, void* cuda_stream) {
@@ -1440,7 +1453,9 @@ int fa_selftest_wait_timeout(unsigned long long limit_ns, void* cuda_stream) {
 
 int fa_smem_bytes(void) { return static_cast<int>(fa::kSmemBytes); }
 
-void fa_set_max_splits(int max_splits) { g_max_splits = max_splits < 0 ? 0 : max_splits; }
+void fa_set_max_splits(int max_splits) {
+  g_max_splits.store(max_splits < 0 ? 0 : max_splits, std::memory_order_relaxed);
+}
 
 int fa_release_workspaces(void) {
   std::lock_guard<std::mutex> lock(g_mutex);
@@ -1448,11 +1463,15 @@ int fa_release_workspaces(void) {
   cudaGetDevice(&prev);
   int rc = FA_OK;
   for (auto& kv : g_workspaces) {
-    if (kv.second.ptr == nullptr) continue;
+    Workspace& w = *kv.second;
+    std::lock_guard<std::mutex> wl(w.mu);
+    if (w.ptr == nullptr) continue;
     cudaError_t e = cudaSetDevice(kv.first.first);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (e == cudaSuccess) e = cudaFree(kv.second.ptr);
+    if (e == cudaSuccess) e = cudaFree(w.ptr);
     if (e != cudaSuccess) rc = set_error(FA_ERR_CUDA, "workspace release: %s", cudaGetErrorString(e));
+    w.ptr = nullptr;
+    w.bytes = 0;
   }
   g_workspaces.clear();
   cudaSetDevice(prev);

@@ -83,11 +83,17 @@ const char* fa_last_error(void);
  * device, synchronising `cuda_stream`. Nonzero bits mean a bounded wait inside
  * a kernel ran out of time and that launch's output is invalid:
  *   1 producer, 2 MMA issuer, 4 softmax, 8 drain, 16 self-test.
+ * There is one status word per device, shared by every stream, thread and
+ * launch on it: a bit set by a launch on one stream is seen (and cleared) by
+ * whichever caller reads next, so the word says that some launch on the
+ * device since the last clear failed, not which one.
  * No counterpart in the reference (its kernel has no waits that can fail).
  */
 int fa_read_status(void* cuda_stream, unsigned int* status_out, int clear);
 
-/* Time limit for every in-kernel wait (default 2 s; 0 restores it). */
+/* Time limit for every in-kernel wait (default 2 s; 0 restores it). The
+ * limit is process-wide: it applies to every later launch from any thread
+ * (the setting itself is atomic). */
 void fa_set_wait_limit_ns(unsigned long long limit_ns);
 
 /*
@@ -111,13 +117,17 @@ int fa_smem_bytes(void);
  * warpgroups take one half of the key range each and merge in the block (no
  * scratch), which measured faster on a B200; k > 1 selects the cross-block
  * split for those problems too.
+ * The policy is process-wide (an atomic setting read by every later launch
+ * from any thread).
  * No counterpart in the reference (its grid never splits the key range).
  */
 void fa_set_max_splits(int max_splits);
 
 /*
  * Synchronises every device that holds a split-mode scratch buffer and frees
- * them all. No counterpart in the reference.
+ * them all, including buffers of streams destroyed since they were made.
+ * Must not run while another thread launches. No counterpart in the
+ * reference.
  */
 int fa_release_workspaces(void);
 

@@ -9,6 +9,14 @@ with the flags of its setup.py (``-O3 --use_fast_math -lineinfo``) and
 so it cannot be confused with this library's ``flash_attention_cuda``).
 Nothing is copied from the reference; the output directory is git-ignored.
 
+It also stages the reference's CPU path, the Python package
+``flash_attention`` (``attention_reference``, flash_attention/reference.py:9-61),
+unmodified into ``baseline/_ref/flash_attention/`` next to the reference's own
+pip-installed extension: the reference's setup.py:5-33 declares no Python
+packages, so ``pip install --target baseline/_ref`` places only the
+extension.  That directory is git-ignored and travels with the working tree,
+so the timed CPU baseline can run the reference's own code on the GPU host.
+
     python oracle/build_ref.py REFERENCE_ROOT
 """
 
@@ -71,7 +79,26 @@ def build(ref_root: Path) -> Path:
     return target
 
 
+BASELINE_REF = HERE.parent / "baseline" / "_ref"
+
+
+def stage_python(ref_root: Path) -> Path:
+    """Copy the reference's ``flash_attention`` package files byte for byte
+    into ``baseline/_ref/flash_attention/`` (git-ignored)."""
+    import shutil
+
+    src = ref_root / "flash_attention"
+    if not (src / "reference.py").is_file():
+        raise FileNotFoundError(f"{src / 'reference.py'} not found")
+    dst = BASELINE_REF / "flash_attention"
+    dst.mkdir(parents=True, exist_ok=True)
+    for f in sorted(src.glob("*.py")):
+        shutil.copyfile(f, dst / f.name)
+    return dst
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         sys.exit(__doc__)
     print(build(Path(sys.argv[1])))
+    print(stage_python(Path(sys.argv[1])))

@@ -104,3 +104,42 @@ def test_drop_in_module_shim():
     import flash_attention_cuda
 
     assert callable(flash_attention_cuda.tensorcore_attention_forward_production_128x128)
+
+
+def test_policy_setters_race_free_with_validating_calls():
+    # One thread flips the process-wide policies (atomic settings) while
+    # another runs the ABI's argument validation; neither may crash, and
+    # every validating call keeps its own error code and per-thread message.
+    import threading
+
+    lib = _native.lib()
+    stop = threading.Event()
+    errors = []
+
+    def setter():
+        i = 0
+        while not stop.is_set():
+            lib.fa_set_max_splits(i % 5)
+            lib.fa_set_wait_limit_ns((i % 3) * 1_000_000)
+            i += 1
+
+    def caller():
+        try:
+            for _ in range(20000):
+                if lib.fa_fwd_sm100(None, None, None, None, -1, 1, 128, 0, 0.125, None) != -1:
+                    errors.append("negative size accepted")
+                if "negative" not in _native.last_error():
+                    errors.append(_native.last_error())
+                if lib.fa_fwd_sm100(8, 16, 32, 48, 1, 1, 128, 0, 0.125, None) != -1:
+                    errors.append("misaligned pointer accepted")
+        finally:
+            stop.set()
+
+    threads = [threading.Thread(target=setter), threading.Thread(target=caller)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    lib.fa_set_max_splits(0)
+    lib.fa_set_wait_limit_ns(0)
+    assert not errors, errors[:3]

@@ -108,3 +108,24 @@ def test_split_layouts_in_sequence():
             ref = attention_oracle(q.float().cpu().numpy(), k.float().cpu().numpy(),
                                    v.float().cpu().numpy(), causal=causal)
             assert_parity(out, ref, what=f"{(b, h, nq, nk, causal)}")
+
+
+def test_split_recovers_after_a_timed_out_launch():
+    # A split launch whose waits run out of time returns early, possibly after
+    # some splits have counted themselves finished.  The counters are cleared
+    # before every split launch, so the next launch on the stream is correct.
+    q, k, v = seeded(1, 2, 4096, 4096, seed=11)
+    lib = _native.lib()
+    try:
+        lib.fa_set_wait_limit_ns(1000)  # 1 us: the pipeline's first waits give up
+        abi_forward(q, k, v, False)
+        torch.cuda.synchronize()
+    finally:
+        lib.fa_set_wait_limit_ns(0)
+    read_status(clear=True)  # may or may not report the time-outs
+    ref = attention_oracle(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                           v.float().cpu().numpy(), causal=False)
+    for _ in range(2):
+        out = abi_forward(q, k, v, False)
+        torch.cuda.synchronize()
+        assert_parity(out, ref, what="split after a timed-out launch")

@@ -32,12 +32,19 @@ def noalloc_forward(q, k, v, causal, scale=None):
 CASES = [(1, 8, 2048, 2048), (1, 1, 8192, 8192), (1, 2, 1000, 6000), (2, 4, 1024, 1024)]
 
 
+@pytest.fixture
+def split_across_blocks():
+    # An explicit split limit: the first three cases use the cross-block split
+    # and its scratch (the automatic policy keeps one-wave problems in-block).
+    # The teardown restores the process-wide policy even when a check fails.
+    _native.lib().fa_set_max_splits(16)
+    yield
+    _native.lib().fa_set_max_splits(0)
+
+
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize(("b", "h", "nq", "nk"), CASES)
-def test_noalloc_matches_regular_entry_point_twice(b, h, nq, nk, causal):
-    # an explicit split limit: the first three cases use the cross-block split
-    # and its scratch (the automatic policy keeps one-wave problems in-block)
-    _native.lib().fa_set_max_splits(16)
+def test_noalloc_matches_regular_entry_point_twice(split_across_blocks, b, h, nq, nk, causal):
     g = torch.Generator().manual_seed(nq + nk + b)
     q = torch.randn(b, h, nq, 64, generator=g).half().cuda()
     k = torch.randn(b, h, nk, 64, generator=g).half().cuda()
@@ -48,5 +55,30 @@ def test_noalloc_matches_regular_entry_point_twice(b, h, nq, nk, causal):
         torch.cuda.synchronize()
         bound = ATOL + RTOL * expected.abs()
         assert ((got - expected).abs() <= bound).all()
-    _native.lib().fa_set_max_splits(0)
+    assert read_status() == 0
+
+
+def test_noalloc_takes_no_device_memory(split_across_blocks):
+    # On a stream that has never run a split launch, the regular entry point
+    # would allocate its scratch buffer (several MiB here); the no-alloc entry
+    # point must leave the device's free memory unchanged.
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn(1, 1, 8192, 64, generator=g).half().cuda() for _ in range(3))
+    out = torch.empty_like(q)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    free_before, _ = torch.cuda.mem_get_info()
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            rc = _native.lib().fa_fwd_sm100_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                    out.data_ptr(), 1, 1, 8192, 8192, 0, 0.125,
+                                                    side.cuda_stream)
+            _native.check(rc)
+    side.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
+    expected = abi_forward(q, k, v, False)
+    torch.cuda.synchronize()
+    bound = ATOL + RTOL * expected.float().abs()
+    assert ((out.float() - expected.float()).abs() <= bound).all()
     assert read_status() == 0
