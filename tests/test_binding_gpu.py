@@ -37,18 +37,52 @@ def test_production_128x128_matches_sdpa(batch, heads, sequence_length, causal):
     assert_parity(actual, ref)
 
 
-@pytest.mark.parametrize(("name", "n"), [
-    ("tensorcore_attention_forward", 80),
-    ("tensorcore_attention_forward_bc32", 96),
-    ("tensorcore_attention_forward_bc32_raw_pv", 160),
-    ("tensorcore_attention_forward_bc32_raw_qk_raw_pv", 256),
-])
-def test_legacy_entry_points_match_sdpa(name, n):
-    torch.manual_seed(1)
-    q, k, v = (torch.randn(2, 3, n, 64, device="cuda", dtype=torch.float16) for _ in range(3))
+# The reference's own shapes for its earlier entry points
+# (tests/test_tensorcore_attention.py:15-24 for the Bc16 kernel, :81-90,
+# :182-191 and :240-249 for the three Bc32 variants); all route to the sm_100a
+# kernel here and are checked against SDPA at the reference's 3e-2 and against
+# the FP32 oracle at the north-star bound.
+BC16_SHAPES = [(1, 1, 16), (1, 2, 64), (1, 4, 80), (1, 8, 128), (2, 3, 256)]
+BC32_SHAPES = [(1, 1, 32), (1, 2, 64), (1, 4, 96), (1, 8, 128), (1, 8, 512)]
+BC32_NAMES = ["tensorcore_attention_forward_bc32", "tensorcore_attention_forward_bc32_raw_pv",
+              "tensorcore_attention_forward_bc32_raw_qk_raw_pv"]
+LEGACY_CASES = ([("tensorcore_attention_forward", *s) for s in BC16_SHAPES]
+                + [(n, *s) for n in BC32_NAMES for s in BC32_SHAPES])
+
+
+@pytest.mark.parametrize(("name", "batch", "heads", "n"), LEGACY_CASES)
+def test_legacy_entry_points_match_sdpa_and_oracle(name, batch, heads, n):
+    torch.manual_seed(n + heads)
+    q, k, v = (torch.randn(batch, heads, n, 64, device="cuda", dtype=torch.float16)
+               for _ in range(3))
     out = getattr(_native.ext(), name)(q, k, v)
+    assert out.shape == q.shape and out.dtype == torch.float16
     exp = F.scaled_dot_product_attention(q, k, v)
     torch.testing.assert_close(out, exp, rtol=3e-2, atol=3e-2)
+    ref = attention_oracle(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                           v.float().cpu().numpy(), causal=False)
+    assert_parity(out, ref, what=f"{name} N={n}")
+
+
+@pytest.mark.parametrize("name", BC32_NAMES)
+def test_bc32_entry_points_reject_partial_key_tile(name):
+    # reference tests/test_tensorcore_attention.py:155-179
+    q = torch.randn(1, 1, 48, 64, device="cuda", dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="divisible by 32"):
+        getattr(_native.ext(), name)(q, torch.randn_like(q), torch.randn_like(q))
+
+
+def test_flash_attention_package_forward_calls():
+    import flash_attention
+
+    torch.manual_seed(3)
+    q, k, v = (torch.randn(2, 4, 384, 64, device="cuda", dtype=torch.float16) for _ in range(3))
+    for causal, fn in ((False, flash_attention.attention_forward),
+                       (True, flash_attention.attention_forward_causal)):
+        out = fn(q, k, v)
+        ref = attention_oracle(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                               v.float().cpu().numpy(), causal=causal)
+        assert_parity(out, ref, what=f"flash_attention causal={causal}")
 
 
 def test_package_calls():
