@@ -503,6 +503,11 @@ def run_ours(args):
     del hq, hk, hv, hout
     link = host_link_ceiling(dev, world, local)
     e2e_gbs = (h2d + d2h) / (e2e_ms / 1e3) / 1e9
+    # The host-link bound of one step: the copies alone at the concurrent
+    # ceilings (each direction on its own, and both together), whichever is
+    # slowest; the kernel itself is far shorter than any of them.
+    link_ms = max(h2d / (link["h2d"] * 1e9), d2h / (link["d2h"] * 1e9),
+                  (h2d + d2h) / (link["both"] * 1e9)) * 1e3
     nodes = max_over_ranks_vec([numa], dev)  # all ranks' nodes agree here or the max shows one
 
     extra = {}
@@ -553,6 +558,8 @@ def run_ours(args):
                 "h2d_ceiling_gbs": link["h2d"], "d2h_ceiling_gbs": link["d2h"],
                 "bidir_ceiling_gbs": link["both"],
                 "frac_of_bidir_ceiling": round(e2e_gbs / link["both"], 4),
+                "link_bound_ms": round(link_ms, 3),
+                "frac_of_link_bound": round(link_ms / e2e_ms, 4),
                 "ceiling": "plain 1 GiB pinned copies on all ranks at once, max-over-ranks time",
                 "numa_node": int(nodes[0]), "bound_cpus": bound_cpus},
         "gpu_launches": args.steps,
