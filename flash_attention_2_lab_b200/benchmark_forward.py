@@ -4,8 +4,13 @@ and its timing method (benchmarks/harness.py:34-71: warm-up, then samples x
 iterations between CUDA events, median / p10 / p90 per call).
 
 Added columns: TFLOPS (4*B*H*Nq*Nk*D, halved for causal) and the fraction of
-the measured B200 peak.  Added mode: ``--gpus N`` splits the (batch, head)
-slices over N devices of this process and reports the slowest device's time.
+the measured B200 peak.  Added modes: ``--gpus N`` splits the (batch, head)
+slices over N devices of this process and reports the slowest device's time;
+``--sustained S`` runs each kernel back to back for S seconds while
+nvidia-smi samples device 0's SM clock and power, and reports the sustained
+TFLOPS with the median clock, the median power and TFLOPS per GHz (the
+per-clock efficiency, which is what decides throughput once a long run sits
+at the board's power limit).
 
     python -m flash_attention_2_lab_b200.benchmark_forward --batch 4 --heads 32 \\
         --query-length 8192 --causal --dtype float16 --kernels sm100 sdpa
@@ -16,6 +21,8 @@ from __future__ import annotations
 import argparse
 import json
 import statistics
+import subprocess
+import time
 from pathlib import Path
 
 import torch
@@ -66,6 +73,49 @@ def time_on_devices(ops, samples, iterations, warmup):
     return out
 
 
+def sustained(ops, seconds):
+    """Back-to-back calls for ``seconds`` with nvidia-smi sampling of device 0.
+    Returns (ms per call, median SM MHz under load, median W, reasons seen)."""
+    for dev, op in ops:
+        with torch.cuda.device(dev):
+            for _ in range(5):
+                op()
+    torch.cuda.synchronize()
+    try:
+        smi = subprocess.Popen(["nvidia-smi", "-i", "0", "--query-gpu=clocks.sm,power.draw,"
+                                "clocks_event_reasons.active", "--format=csv,noheader,nounits",
+                                "-lms", "100"], stdout=subprocess.PIPE, text=True)
+    except OSError:
+        smi = None
+    time.sleep(0.3)
+    calls = 0
+    start = time.perf_counter()
+    while time.perf_counter() - start < seconds:
+        for _ in range(10):
+            for dev, op in ops:
+                with torch.cuda.device(dev):
+                    op()
+        calls += 10
+        torch.cuda.synchronize()
+    elapsed = time.perf_counter() - start
+    mhz, watts, reasons = [], [], set()
+    if smi is not None:
+        smi.terminate()
+        for row in smi.communicate()[0].strip().splitlines():
+            parts = [x.strip() for x in row.split(",")]
+            if len(parts) != 3:
+                continue
+            try:
+                mhz.append(float(parts[0]))
+                watts.append(float(parts[1]))
+            except ValueError:
+                continue
+            reasons.add(parts[2])
+    loaded = [m for m in mhz if m > 0.5 * max(mhz)] if mhz else []
+    return (elapsed * 1e3 / calls, statistics.median(loaded) if loaded else None,
+            statistics.median(watts) if watts else None, sorted(reasons))
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=1)
@@ -82,6 +132,8 @@ def main(argv=None) -> None:
                     help="kernel names: sm100 (this library), sdpa (PyTorch, for context)")
     ap.add_argument("--gpus", type=int, default=1, help="devices to split (b, h) over")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--sustained", type=float, default=0.0,
+                    help="seconds of back-to-back calls per kernel with clock/power sampling")
     args = ap.parse_args(argv)
 
     nk = args.key_length if args.key_length is not None else args.query_length
@@ -126,6 +178,15 @@ def main(argv=None) -> None:
             print(f"{name:10s} unsupported for this dtype / head dimension")
             continue
         ops = [(dev, mk(dq, dk, dv)) for dev, dq, dk, dv in shards]
+        if args.sustained > 0:
+            with torch.inference_mode():
+                ms, mhz, watts, reasons = sustained(ops, args.sustained)
+            tf = flops / (ms / 1e3) / 1e12
+            per_ghz = tf / (mhz / 1e3) if mhz else float("nan")
+            print(f"{name:10s} sustained {args.sustained:.0f} s: {ms:.4f} ms/call, {tf:.1f} TFLOPS, "
+                  f"SM {mhz} MHz (median), {watts} W (median), {per_ghz:.1f} TFLOPS/GHz, "
+                  f"clock event reasons {reasons}")
+            continue
         with torch.inference_mode():
             ms = time_on_devices(ops, args.samples, args.iterations, args.warmup)
         med = statistics.median(ms)

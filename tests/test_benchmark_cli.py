@@ -18,3 +18,11 @@ def test_cli_runs_small_case(capsys):
                             "--warmup", "3", "--kernels", "sm100", "sdpa"])
     out = capsys.readouterr().out
     assert "sm100" in out and "TFLOPS" in out and "sdpa / sm100" in out
+
+
+@pytest.mark.gpu
+def test_cli_sustained_mode(capsys):
+    benchmark_forward.main(["--batch", "1", "--heads", "8", "--query-length", "1024",
+                            "--kernels", "sm100", "--sustained", "1"])
+    out = capsys.readouterr().out
+    assert "sustained" in out and "TFLOPS/GHz" in out
