@@ -10,14 +10,20 @@ Public calls (all run the sm_100a kernel; there is no CPU or eager fallback):
   any sequence length, different query/key lengths, optional scale.
 * ``attention_forward_causal(q, k, v)`` -- the causal call.
 * ``sharded`` -- (batch, head) sharding of one forward over several GPUs.
+* ``attention(q, k, v, causal=False, scale=None)`` -- differentiable form
+  (forward with log-sum-exp, backward kernel); see ``autograd``.
 """
 
 from __future__ import annotations
 
 from ._native import ext, lib
+from .autograd import attention, attention_backward, attention_forward_lse
 
 __all__ = [
+    "attention",
+    "attention_backward",
     "attention_forward",
+    "attention_forward_lse",
     "attention_forward_causal",
     "tensorcore_attention_forward_production_128x128",
     "ext",

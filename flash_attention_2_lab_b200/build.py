@@ -54,7 +54,8 @@ def _run(cmd: list[str]) -> None:
 
 
 def build_lib(force: bool = False, verbose_ptxas: bool = False) -> Path:
-    sources = [CSRC / "fa_fwd_sm100.cu", CSRC / "sm100_ptx.cuh", INCLUDE / "fa_sm100.h"]
+    sources = [CSRC / "fa_fwd_sm100.cu", CSRC / "fa_bwd_sm100.cuh", CSRC / "sm100_ptx.cuh",
+               INCLUDE / "fa_sm100.h"]
     if force or _stale(LIB, sources):
         nvcc = str(_cuda_home() / "bin" / "nvcc")
         cmd = [nvcc, *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",

@@ -1,0 +1,413 @@
+// Attention backward for B200 (sm_100a), head dimension 64, fp16 inputs and
+// gradients, fp32 accumulation.  Included by fa_fwd_sm100.cu (it shares the
+// PTX wrappers, the status word and the host plumbing there).
+//
+// Not in the reference (its kernels are forward only); this is the training
+// half of the same attention: given Q, K, V, O, dO and the forward's row
+// log-sum-exp L,
+//   P  = exp(scale * Q K^T - L)          (recomputed, causal mask applied)
+//   dV = P^T dO,   dP = dO V^T,   dS = P * (dP - D),   D = rowsum(dO * O)
+//   dK = scale * dS^T Q,          dQ = scale * dS K
+//
+// One block per (batch*head, 128-key tile j); it keeps K_j, V_j, dK_j and dV_j
+// on chip and walks the query tiles i (all of them, or i >= j when causal):
+//
+//   warp 4   TMA producer: K_j, V_j once; per query tile Q_i, dO_i and the
+//            row terms (L * log2 e, D) into a two-slot ring.
+//   warp 5   MMA issuer and TMEM owner.  Per query tile:
+//              S^T  = K_j Q_i^T   (SS, 128 keys x 128 queries)     -> TMEM
+//              dP^T = V_j dO_i^T  (SS)                              -> TMEM
+//            then, once the compute warps have written P^T and dS^T,
+//              dV  += P^T  dO_i   (TS, P^T read from TMEM)
+//              dK  += dS^T Q_i    (TS, dS^T read from TMEM)
+//              dQ_i = dS K_j      (SS; dS^T staged in shared memory is read
+//                                  as an MN-major A operand)
+//   warps 0-3  compute, one thread per TMEM lane: for key row k, the 128
+//            queries of the tile: p = 2^(s c - L log2 e), ds = p (dp - D),
+//            both to fp16 into TMEM (and ds into shared memory); then, with
+//            the lane now a query row, the fp32 dQ_i tile is added into a
+//            global fp32 accumulator with vector reductions (the other key
+//            tiles add theirs).
+//
+// Tensor memory (512 columns): S^T 0-127 (dQ_i reuses 0-63 once S^T is
+// consumed), dP^T 128-255, P^T 256-319 (fp16 pairs), dS^T 320-383 (fp16
+// pairs), dV 384-447, dK 448-511.
+//
+// Shared-memory descriptors of MN-major operands (128-byte swizzle): an atom
+// is 8 rows of the K dimension x 64 fp16 of the MN dimension (128 B per
+// row); the leading byte offset is the stride between atoms along MN and the
+// stride byte offset the stride between 8-row groups along K.
+//
+// Every wait is bounded, as in the forward kernel.
+#pragma once
+
+namespace fa {
+namespace bwd {
+
+constexpr int kThreads = 192;
+constexpr int kQSlots = 2;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+
+constexpr uint32_t kSmK = 0;
+constexpr uint32_t kSmV = kSmK + kTileBytes;
+constexpr uint32_t kSmQ = kSmV + kTileBytes;
+constexpr uint32_t kSmDO = kSmQ + kQSlots * kTileBytes;
+constexpr uint32_t kSmDS = kSmDO + kQSlots * kTileBytes;  // two 64-query halves, 16 KiB each
+constexpr uint32_t kSmVec = kSmDS + 2 * kTileBytes;       // per slot: 128 x (L log2 e, D)
+constexpr uint32_t kVecBytes = 128 * 2 * sizeof(float);
+constexpr uint32_t kSmCtl = kSmVec + kQSlots * kVecBytes;
+constexpr uint32_t kSmBytes = kSmCtl + 256 + 1024;  // + alignment slack
+
+constexpr uint32_t kColS = 0, kColDP = 128, kColP = 256, kColDS = 320, kColDV = 384,
+                   kColDK = 448;
+
+struct Ctl {
+  uint64_t kv_full;
+  uint64_t q_full[kQSlots], q_empty[kQSlots];
+  uint64_t s_full, p_full, dq_full, dq_free;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(Ctl) <= 256, "control block too large");
+
+struct Params {
+  int n;             // query and key rows per (batch, head)
+  int n_pad;         // n rounded up to 128 (rows of the row-term and dQ buffers)
+  int bh;
+  int causal;
+  int n_kt;          // key (and query) tiles per (batch, head)
+  float scale;       // softmax scale
+  float scale_log2;  // scale * log2(e)
+  const float2* rowterm;  // [bh][n_pad]: (L log2 e, D)
+  float* dq_acc;          // [bh][n_pad][64] fp32, zeroed before the launch
+  __half* dk;             // [bh][n][64]
+  __half* dv;
+  unsigned int* status;
+  unsigned long long limit_ns;
+};
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+// First query tile of key tile j (top-left causal mask: key k is seen by
+// queries q >= k, i.e. query tiles i >= j).
+__device__ __forceinline__ int first_qtile(const Params& p, int j) { return p.causal ? j : 0; }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+               const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // SW128 tiles need 1 KiB alignment
+  uint8_t* gen_base = smem_raw + (base - raw);
+  Ctl* ctl = reinterpret_cast<Ctl*>(gen_base + kSmCtl);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // heaviest blocks (small j under the causal mask) first
+  const int bh = blockIdx.x / p.n_kt;
+  const int j = blockIdx.x % p.n_kt;
+  const int i0 = first_qtile(p, j);
+  const int n_steps = p.n_kt - i0;
+  volatile int* abort_flag = &ctl->abort;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&ctl->kv_full), 1);
+    for (int s = 0; s < kQSlots; ++s) {
+      mbar_init(smem_u32(&ctl->q_full[s]), 1);
+      mbar_init(smem_u32(&ctl->q_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&ctl->s_full), 1);
+    mbar_init(smem_u32(&ctl->p_full), 4);
+    mbar_init(smem_u32(&ctl->dq_full), 1);
+    mbar_init(smem_u32(&ctl->dq_free), 4);
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      const uint32_t kv = smem_u32(&ctl->kv_full);
+      mbar_arrive_expect_tx(kv, 2 * kTileBytes);
+      tma_load_3d(base + kSmK, &tm_k, kv, 0, j * 128, bh);
+      tma_load_3d(base + kSmV, &tm_v, kv, 0, j * 128, bh);
+    }
+    __syncwarp();
+    int issued = 0;
+    for (int it = 0; it < n_steps; ++it) {
+      const int i = i0 + it, slot = it % kQSlots;
+      if (!mbar_wait_warp(smem_u32(&ctl->q_empty[slot]), ((it / kQSlots) & 1) ^ 1, abort_flag,
+                          p.status, kStatusTimeoutProducer, p.limit_ns))
+        break;
+      if (elect_one()) {
+        const uint32_t full = smem_u32(&ctl->q_full[slot]);
+        mbar_arrive_expect_tx(full, 2 * kTileBytes + kVecBytes);
+        tma_load_3d(base + kSmQ + slot * kTileBytes, &tm_q, full, 0, i * 128, bh);
+        tma_load_3d(base + kSmDO + slot * kTileBytes, &tm_do, full, 0, i * 128, bh);
+        bulk_load(base + kSmVec + slot * kVecBytes,
+                  p.rowterm + static_cast<size_t>(bh) * p.n_pad + i * 128, kVecBytes, full);
+      }
+      __syncwarp();
+      issued = it + 1;
+    }
+    // Let every copy started land before the block exits (bounded).
+    if (lane == 0) {
+      mbar_wait(smem_u32(&ctl->kv_full), 0, nullptr, p.status, kStatusTimeoutDrain,
+                kDrainLimitNs);
+      for (int it = issued - 1; it >= 0 && it >= issued - kQSlots; --it)
+        mbar_wait(smem_u32(&ctl->q_full[it % kQSlots]), (it / kQSlots) & 1, nullptr, p.status,
+                  kStatusTimeoutDrain, kDrainLimitNs);
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = idesc_f16_f32(128, 128, false);
+    constexpr uint32_t idesc_g = idesc_f16_f32(128, 64, true);  // B (dO, Q) MN-major
+    // dQ = dS K: A = dS read MN-major (queries contiguous), B = K MN-major.
+    constexpr uint32_t idesc_dq = idesc_f16_f32(128, 64, true) | (1u << 15);
+    const uint64_t dk_ = smem_desc_sw128(base + kSmK, 16, 1024);
+    const uint64_t dv_ = smem_desc_sw128(base + kSmV, 16, 1024);
+    const uint64_t dds = smem_desc_sw128(base + kSmDS, kTileBytes, 1024);
+    constexpr uint64_t kTileDesc = kTileBytes >> 4;
+    auto wait = [&](uint32_t bar, uint32_t parity) {
+      return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutMma, p.limit_ns);
+    };
+    bool ok = wait(smem_u32(&ctl->kv_full), 0);
+    for (int it = 0; ok && it < n_steps; ++it) {
+      const int slot = it % kQSlots;
+      if (!wait(smem_u32(&ctl->q_full[slot]), (it / kQSlots) & 1)) break;
+      // S^T is written over the previous dQ tile: it must have been read
+      if (it > 0 && !wait(smem_u32(&ctl->dq_free), (it - 1) & 1)) break;
+      tc_fence_after();
+      const uint64_t dq_ = smem_desc_sw128(base + kSmQ, 16, 1024) + slot * kTileDesc;
+      const uint64_t ddo = smem_desc_sw128(base + kSmDO, 16, 1024) + slot * kTileDesc;
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss_f16(tmem + kColS, dk_ + 2 * kk, dq_ + 2 * kk, idesc_s, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss_f16(tmem + kColDP, dv_ + 2 * kk, ddo + 2 * kk, idesc_s, kk > 0);
+        tc_commit(smem_u32(&ctl->s_full));
+      }
+      __syncwarp();
+      if (!wait(smem_u32(&ctl->p_full), it & 1)) break;
+      tc_fence_after();
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 16 queries per step
+          mma_ts_f16(tmem + kColDV, tmem + kColP + kk * 8, ddo + 128 * kk, idesc_g,
+                     (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts_f16(tmem + kColDK, tmem + kColDS + kk * 8, dq_ + 128 * kk, idesc_g,
+                     (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 16 keys per step
+          mma_ss_f16(tmem + kColS, dds + 128 * kk, dk_ + 128 * kk, idesc_dq, kk > 0);
+        tc_commit(smem_u32(&ctl->dq_full));
+        tc_commit(smem_u32(&ctl->q_empty[slot]));
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      tc_commit(smem_u32(&ctl->drain));
+      mbar_wait(smem_u32(&ctl->drain), 0, nullptr, p.status, kStatusTimeoutDrain, kDrainLimitNs);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ compute
+    const int r = warp * 32 + lane;  // TMEM lane: key row, then query row of dQ
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + kColS, t_dp = tmem + lane_base + kColDP;
+    const uint32_t t_p = tmem + lane_base + kColP, t_ds = tmem + lane_base + kColDS;
+    const int key = j * 128 + r;
+    const float c = p.scale_log2;
+    auto wait = [&](uint32_t bar, uint32_t parity) {
+      return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax,
+                            p.limit_ns);
+    };
+    bool ok = true;
+    for (int it = 0; it < n_steps; ++it) {
+      const int i = i0 + it, slot = it % kQSlots;
+      if (!wait(smem_u32(&ctl->q_full[slot]), (it / kQSlots) & 1)) { ok = false; break; }
+      if (!wait(smem_u32(&ctl->s_full), it & 1)) { ok = false; break; }
+      tc_fence_after();
+      const float2* rt = reinterpret_cast<const float2*>(gen_base + kSmVec + slot * kVecBytes);
+      // keys past n and (causal) queries before this key contribute nothing
+      const int q_lo = p.causal ? key : 0;  // first query that sees this key
+      const bool key_ok = key < p.n;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sr[32], dpr[32];
+        tmem_ld32(t_s + 32 * ch, sr);
+        tmem_ld32(t_dp + 32 * ch, dpr);
+        tc_wait_ld();
+        uint32_t pk[16], dk16[16];
+#pragma unroll
+        for (int u = 0; u < 32; u += 2) {
+          const int ql = 32 * ch + u;  // query within the tile
+          const float4 t2 = *reinterpret_cast<const float4*>(rt + ql);  // (L2, D) of ql, ql+1
+          const int q = i * 128 + ql;
+          float p0 = ex2_approx(__uint_as_float(sr[u]) * c - t2.x);
+          float p1 = ex2_approx(__uint_as_float(sr[u + 1]) * c - t2.z);
+          if (!key_ok || q < q_lo || q >= p.n) p0 = 0.f;
+          if (!key_ok || q + 1 < q_lo || q + 1 >= p.n) p1 = 0.f;
+          const float d0 = p0 * (__uint_as_float(dpr[u]) - t2.y);
+          const float d1 = p1 * (__uint_as_float(dpr[u + 1]) - t2.w);
+          pk[u / 2] = pack_half2(p0, p1);
+          dk16[u / 2] = pack_half2(d0, d1);
+        }
+        tmem_st16(t_p + 16 * ch, pk);
+        tmem_st16(t_ds + 16 * ch, dk16);
+        // dS^T row r, queries 32 ch .. 32 ch + 31: half ch / 2 of the staged
+        // tile, four 16-byte chunks of its 128-byte row (128B swizzle)
+        const uint32_t row_addr = base + kSmDS + (ch / 2) * kTileBytes + r * 128;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int chunk = (ch % 2) * 4 + q4;
+          const uint32_t dst = row_addr + ((chunk ^ (r & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(dk16[4 * q4]),
+                       "r"(dk16[4 * q4 + 1]), "r"(dk16[4 * q4 + 2]), "r"(dk16[4 * q4 + 3])
+                       : "memory");
+        }
+      }
+      tc_wait_st();
+      fence_proxy_async_smem();  // dS^T in shared memory is read by the MMA (async proxy)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->p_full));
+      // ---- dQ_i (lane = query row) into the fp32 accumulator
+      if (!wait(smem_u32(&ctl->dq_full), it & 1)) { ok = false; break; }
+      tc_fence_after();
+      const int q = i * 128 + r;
+      float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.n_pad + q) * 64;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t dq[32];
+        tmem_ld32(t_s + 32 * h, dq);
+        tc_wait_ld32(dq);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          red_add_v4(dst + 32 * h + 4 * e, __uint_as_float(dq[4 * e]),
+                     __uint_as_float(dq[4 * e + 1]), __uint_as_float(dq[4 * e + 2]),
+                     __uint_as_float(dq[4 * e + 3]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));
+    }
+    // ---- dK_j, dV_j (lane = key row): after the last dQ, every MMA is done
+    if (ok && n_steps > 0 && key < p.n) {
+      const size_t row = static_cast<size_t>(bh) * p.n + key;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t col = which ? kColDK : kColDV;
+        const float mul = which ? p.scale : 1.f;
+        __half* out = (which ? p.dk : p.dv) + row * 64;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t g[32];
+          tmem_ld32(tmem + lane_base + col + 32 * h, g);
+          tc_wait_ld32(g);
+          uint32_t hv[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            hv[e] = pack_half2(__uint_as_float(g[2 * e]) * mul, __uint_as_float(g[2 * e + 1]) * mul);
+          uint4* o4 = reinterpret_cast<uint4*>(out + 32 * h);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            o4[e] = make_uint4(hv[4 * e], hv[4 * e + 1], hv[4 * e + 2], hv[4 * e + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Row terms for the backward: (L log2 e, D = rowsum(dO * O)) per query row,
+// zero for the padding rows up to n_pad.  One thread per row.
+__global__ void rowterm_kernel(const __half* __restrict__ o, const __half* __restrict__ d_o,
+                               const float* __restrict__ lse, float2* __restrict__ rowterm,
+                               int n, int n_pad, int64_t rows_pad) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= rows_pad) return;
+  const int64_t bh = idx / n_pad;
+  const int q = static_cast<int>(idx - bh * n_pad);
+  float2 out = make_float2(0.f, 0.f);
+  if (q < n) {
+    const size_t row = static_cast<size_t>(bh) * n + q;
+    const uint4* a = reinterpret_cast<const uint4*>(o + row * 64);
+    const uint4* b = reinterpret_cast<const uint4*>(d_o + row * 64);
+    float acc = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint4 va = a[e], vb = b[e];
+      const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&wa[w]));
+        const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&wb[w]));
+        acc = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, acc));
+      }
+    }
+    out = make_float2(lse[row] * 1.4426950408889634f, acc);
+  }
+  rowterm[idx] = out;
+}
+
+// dq = scale * dq_acc, fp32 -> fp16, rows below n.
+__global__ void dq_convert_kernel(const float* __restrict__ dq_acc, __half* __restrict__ dq,
+                                  int n, int n_pad, int64_t rows, float scale) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (row, 8-col group)
+  if (idx >= rows * 8) return;
+  const int64_t row = idx / 8;
+  const int g = static_cast<int>(idx % 8);
+  const int64_t bh = row / n;
+  const int q = static_cast<int>(row - bh * n);
+  const float4* src =
+      reinterpret_cast<const float4*>(dq_acc + (static_cast<size_t>(bh) * n_pad + q) * 64 + 8 * g);
+  const float4 a = src[0], b = src[1];
+  uint4 out;
+  out.x = pack_half2(a.x * scale, a.y * scale);
+  out.y = pack_half2(a.z * scale, a.w * scale);
+  out.z = pack_half2(b.x * scale, b.y * scale);
+  out.w = pack_half2(b.z * scale, b.w * scale);
+  reinterpret_cast<uint4*>(dq + row * 64)[g] = out;
+}
+
+}  // namespace bwd
+}  // namespace fa

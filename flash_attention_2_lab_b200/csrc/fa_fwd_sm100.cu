@@ -168,6 +168,8 @@ struct FwdParams {
   unsigned int* status;
   unsigned long long limit_ns;
   float* dbg;       // optional: first item's first masked score tile (tests)
+  float* lse;       // optional: [bh][n_q] row log-sum-exp of the scaled scores (natural log)
+  float scale;      // softmax scale (for the log-sum-exp)
   // Key-range split (n_split > 1): a work item is (bh, query pair, split);
   // each split writes fp32 partial results and the last split to finish a
   // query tile merges them.  The three arrays live in one scratch buffer.
@@ -535,7 +537,7 @@ __device__ bool mma_loop_halves(const FwdParams& p, SharedCtl* ctl, uint32_t sme
   return true;
 }
 
-template <bool kSplit, bool kTurnsAlways, bool kHalves>
+template <bool kSplit, bool kTurnsAlways, bool kHalves, bool kLse>
 __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_base,
                              uint32_t tmem, const CUtensorMap* tm_o, int t, int warp_in_group,
                              int lane) {
@@ -650,6 +652,9 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
       }
     }
     const int qr = s.q0[t] + row;
+    if constexpr (kLse) {
+      if (qr < p.n_q) p.lse[static_cast<size_t>(s.bh) * p.n_q + qr] = mmax * p.scale + logf(den);
+    }
     if (qr < p.n_q) {
       const float inv = 1.f / den;
       uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(s.bh) * p.n_q + qr) *
@@ -842,6 +847,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
         const float m = fmaxf(m_used, m1);
         const float w0 = ex2_approx((m_used - m) * c), w1 = ex2_approx((m1 - m) * c);
         l = l * w0 + l1 * w1;
+        m_used = m;
         const uint32_t t_o1 = tmem + lane_base + col_o(1);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -875,6 +881,10 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
     }
 
     const float inv = 1.f / l;
+    if constexpr (kLse) {
+      const int qr = s.q0[t] + row;
+      if (qr < p.n_q) p.lse[static_cast<size_t>(s.bh) * p.n_q + qr] = m_used * p.scale + logf(l);
+    }
     uint32_t h[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i)
@@ -910,7 +920,7 @@ __device__ bool softmax_loop(const FwdParams& p, SharedCtl* ctl, uint32_t smem_b
 // is split between the two softmax warpgroups and merged in the block (short
 // problems).  Separate instantiations keep the split merge and the per-item
 // turn check out of the main path's code.
-template <bool kSplit, bool kTurnsAlways, bool kHalves>
+template <bool kSplit, bool kTurnsAlways, bool kHalves, bool kLse = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -964,7 +974,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // up: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
     asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     const bool ok =
-        softmax_loop<kSplit, kTurnsAlways, kHalves>(p, ctl, smem_base, tmem, &tm_o, warp / 4,
+        softmax_loop<kSplit, kTurnsAlways, kHalves, kLse>(p, ctl, smem_base, tmem, &tm_o, warp / 4,
                                                     warp % 4, lane);
     (void)ok;
     if (lane == 0) bulk_wait_group0();  // this warp's output stores
@@ -1034,6 +1044,12 @@ __global__ void selftest_timeout_kernel(unsigned int* status, unsigned long long
 }
 
 __device__ unsigned int g_status_word;
+
+}  // namespace fa
+
+#include "fa_bwd_sm100.cuh"
+
+namespace fa {
 
 // Scratch of fa_fwd_sm100_noalloc: a fixed array that exists on every device
 // that loads this library, for callers that cannot allocate.  12 MiB covers
@@ -1204,11 +1220,19 @@ int ensure_device(int dev, DeviceState** out) {
     for (const void* fn : {reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, true, false>),
                            reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false, false>),
                            reinterpret_cast<const void*>(&fa::fa_fwd_kernel<true, false, false>),
-                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false, true>)}) {
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false, true>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, true, false, true>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false, false, true>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<true, false, false, true>),
+                           reinterpret_cast<const void*>(&fa::fa_fwd_kernel<false, false, true, true>)}) {
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(fa::kSmemBytes));
       if (e != cudaSuccess) break;
     }
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&fa::bwd::bwd_kernel),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(fa::bwd::kSmBytes));
     if (e != cudaSuccess)
       return set_error(FA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     void* sym = nullptr;
@@ -1273,7 +1297,7 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t slices,
 
 int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int64_t n_q,
            int64_t n_k, int causal, float scale, cudaStream_t stream, float* dbg,
-           bool noalloc = false) {
+           bool noalloc = false, float* lse = nullptr) {
   if (bh < 0 || n_q < 0 || n_k < 0) return set_error(FA_ERR_INVALID, "negative size");
   if (bh == 0 || n_q == 0) return FA_OK;
   if (n_k == 0) return set_error(FA_ERR_INVALID, "key length must be positive when queries exist");
@@ -1313,6 +1337,8 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   p.status = d->status;
   p.limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
   p.dbg = dbg;
+  p.lse = lse;
+  p.scale = scale;
 
   p.out = static_cast<__half*>(o);
   const SplitPlan sp = plan_split(bh, n_q, n_k, d->sms);
@@ -1360,7 +1386,17 @@ int launch(const void* q, const void* k, const void* v, void* o, int64_t bh, int
   const int grid = units < d->sms ? units : d->sms;
   constexpr int kThr = fa::kNumThreads;
   constexpr uint32_t kSm = fa::kSmemBytes;
-  if (p.n_split > 1) {
+  if (lse != nullptr) {
+    // the same four variants, each also writing the row log-sum-exp
+    if (p.n_split > 1)
+      fa::fa_fwd_kernel<true, false, false, true><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
+    else if (p.single && FA_HALVES)
+      fa::fa_fwd_kernel<false, false, true, true><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
+    else if (!p.single && sp.n_qtiles % 2 == 0)
+      fa::fa_fwd_kernel<false, true, false, true><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
+    else
+      fa::fa_fwd_kernel<false, false, false, true><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
+  } else if (p.n_split > 1) {
     fa::fa_fwd_kernel<true, false, false><<<grid, kThr, kSm, stream>>>(tq, tk, tv, to, p);
   } else if (p.single && FA_HALVES) {
     // one query tile per block, its key range shared by both softmax warpgroups
@@ -1401,6 +1437,91 @@ int fa_fwd_sm100_noalloc(const void* q, const void* k, const void* v, void* o, i
   if (batch < 0 || heads < 0) return set_error(FA_ERR_INVALID, "negative size");
   return launch(q, k, v, o, batch * heads, q_len, kv_len, causal, scale,
                 static_cast<cudaStream_t>(cuda_stream), nullptr, /*noalloc=*/true);
+}
+
+int fa_fwd_sm100_lse(const void* q, const void* k, const void* v, void* o, float* lse,
+                     int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int causal,
+                     float scale, void* cuda_stream) {
+  if (batch < 0 || heads < 0) return set_error(FA_ERR_INVALID, "negative size");
+  if (lse == nullptr && batch * heads * q_len > 0) return set_error(FA_ERR_INVALID, "null pointer");
+  return launch(q, k, v, o, batch * heads, q_len, kv_len, causal, scale,
+                static_cast<cudaStream_t>(cuda_stream), nullptr, false, lse);
+}
+
+int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                 const float* lse, void* dq, void* dk, void* dv, int64_t batch, int64_t heads,
+                 int64_t seq_len, int causal, float scale, void* cuda_stream) {
+  if (batch < 0 || heads < 0 || seq_len < 0) return set_error(FA_ERR_INVALID, "negative size");
+  const int64_t bh = batch * heads, n = seq_len;
+  if (bh == 0 || n == 0) return FA_OK;
+  const void* ptrs[] = {q, k, v, o, d_o, lse, dq, dk, dv};
+  for (const void* ptr : ptrs) {
+    if (ptr == nullptr) return set_error(FA_ERR_INVALID, "null pointer");
+    if (reinterpret_cast<uintptr_t>(ptr) & 15)
+      return set_error(FA_ERR_INVALID, "tensors must be 16-byte aligned");
+  }
+  if (n > (1ll << 30) || bh > (1ll << 30)) return set_error(FA_ERR_INVALID, "size too large");
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return set_error(FA_ERR_INVALID, "scale must be positive and finite");
+  const int64_t n_kt = (n + 127) / 128, n_pad = n_kt * 128;
+  if (bh * n_kt > 0x7fffffffll) return set_error(FA_ERR_INVALID, "too many blocks");
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  DeviceState* d = nullptr;
+  int rc = ensure_device(dev, &d);
+  if (rc != FA_OK) return rc;
+
+  // scratch: [counter prefix of the split mode, left alone][row terms][dQ accumulator]
+  const size_t rowterm_bytes = align256(static_cast<size_t>(bh) * n_pad * sizeof(float2));
+  const size_t dq_bytes = static_cast<size_t>(bh) * n_pad * 64 * sizeof(float);
+  void* ws = nullptr;
+  if ((rc = get_workspace(dev, stream, kCounterBytes + rowterm_bytes + dq_bytes, &ws)) != FA_OK)
+    return rc;
+  uint8_t* wb = static_cast<uint8_t*>(ws) + kCounterBytes;
+  float2* rowterm = reinterpret_cast<float2*>(wb);
+  float* dq_acc = reinterpret_cast<float*>(wb + rowterm_bytes);
+  e = cudaMemsetAsync(dq_acc, 0, dq_bytes, stream);
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "dQ clear: %s", cudaGetErrorString(e));
+
+  const int64_t rows_pad = bh * n_pad;
+  fa::bwd::rowterm_kernel<<<static_cast<unsigned>((rows_pad + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __half*>(o), static_cast<const __half*>(d_o), lse, rowterm,
+      static_cast<int>(n), static_cast<int>(n_pad), rows_pad);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+
+  CUtensorMap tq, tk, tv, tdo;
+  if ((rc = make_map(&tq, q, n, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tk, k, n, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tv, v, n, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tdo, d_o, n, bh, 128)) != FA_OK) return rc;
+  fa::bwd::Params bp;
+  bp.n = static_cast<int>(n);
+  bp.n_pad = static_cast<int>(n_pad);
+  bp.bh = static_cast<int>(bh);
+  bp.causal = causal ? 1 : 0;
+  bp.n_kt = static_cast<int>(n_kt);
+  bp.scale = scale;
+  bp.scale_log2 = scale * 1.4426950408889634f;
+  bp.rowterm = rowterm;
+  bp.dq_acc = dq_acc;
+  bp.dk = static_cast<__half*>(dk);
+  bp.dv = static_cast<__half*>(dv);
+  bp.status = d->status;
+  bp.limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  fa::bwd::bwd_kernel<<<static_cast<unsigned>(bh * n_kt), fa::bwd::kThreads, fa::bwd::kSmBytes,
+                        stream>>>(tq, tk, tv, tdo, bp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+
+  const int64_t rows = bh * n;
+  fa::bwd::dq_convert_kernel<<<static_cast<unsigned>((rows * 8 + 255) / 256), 256, 0, stream>>>(
+      dq_acc, static_cast<__half*>(dq), static_cast<int>(n), static_cast<int>(n_pad), rows, scale);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return FA_OK;
 }
 
 int fa_fwd_sm100_debug(const void* q, const void* k, const void* v, void* o, int64_t batch,

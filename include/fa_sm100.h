@@ -75,6 +75,35 @@ int fa_fwd_sm100_noalloc(const void* q, const void* k, const void* v, void* o, i
                          int64_t heads, int64_t q_len, int64_t kv_len, int causal, float scale,
                          void* cuda_stream);
 
+/*
+ * As fa_fwd_sm100_varlen, and also writes the row log-sum-exp of the scaled
+ * scores, lse[b, h, i] = log(sum_j exp(scale * q_i . k_j)) over the unmasked
+ * keys (natural log, fp32, contiguous [batch, heads, q_len]), which the
+ * backward pass (fa_bwd_sm100) takes as its softmax statistics.
+ * No counterpart in the reference (its forward returns only O; a training
+ * caller needs the statistics).
+ */
+int fa_fwd_sm100_lse(const void* q, const void* k, const void* v, void* o, float* lse,
+                     int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int causal,
+                     float scale, void* cuda_stream);
+
+/*
+ * Attention backward, head dimension 64, equal query and key lengths:
+ * given q, k, v, the forward output o, the output gradient d_o (all fp16
+ * [batch, heads, seq_len, 64]) and the forward's lse (fp32 [batch, heads,
+ * seq_len], from fa_fwd_sm100_lse), writes dq, dk, dv (fp16, same layout):
+ *   P = exp(scale * Q K^T - lse) (causal: key > query masked),
+ *   dV = P^T dO,  dP = dO V^T,  dS = P * (dP - rowsum(dO * O)),
+ *   dQ = scale * dS K,  dK = scale * dS^T Q.
+ * Uses the scratch buffer per (device, stream) of the split mode for the
+ * fp32 dQ accumulator and the row terms (allocated or grown on first need,
+ * so the first call on a stream allocates).
+ * No counterpart in the reference (it has no backward).
+ */
+int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                 const float* lse, void* dq, void* dk, void* dv, int64_t batch, int64_t heads,
+                 int64_t seq_len, int causal, float scale, void* cuda_stream);
+
 /* Message for the last failing call on this thread ("" if none). */
 const char* fa_last_error(void);
 

@@ -143,3 +143,17 @@ def test_policy_setters_race_free_with_validating_calls():
     lib.fa_set_max_splits(0)
     lib.fa_set_wait_limit_ns(0)
     assert not errors, errors[:3]
+
+
+def test_training_entry_points_validate_without_gpu():
+    lib = _native.lib()
+    assert lib.fa_bwd_sm100(None, None, None, None, None, None, None, None, None, 0, 4, 128, 0,
+                            0.125, None) == 0
+    assert lib.fa_bwd_sm100(None, None, None, None, None, None, None, None, None, 1, 1, 128, 0,
+                            0.125, None) == -1
+    assert "null" in _native.last_error()
+    assert lib.fa_fwd_sm100_lse(16, 16, 16, 16, None, 1, 1, 128, 128, 0, 0.125, None) == -1
+    ext = _native.ext()
+    x = torch.zeros(1, 1, 128, 64, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="query must be a CUDA tensor"):
+        ext.attention_forward_lse(x, x, x, False, None)
