@@ -324,9 +324,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));
     }
-    // ---- dK_j, dV_j (lane = key row): after the last dQ, every MMA is done
-    if (ok && n_steps > 0 && key < p.n) {
-      const size_t row = static_cast<size_t>(bh) * p.n + key;
+    // ---- dK_j, dV_j (lane = key row): after the last dQ, every MMA is done.
+    // The TMEM loads are warp-collective: every lane takes part, only the
+    // lanes of keys below n store.
+    if (ok) {
+      const size_t row = static_cast<size_t>(bh) * p.n + (key < p.n ? key : 0);
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint32_t col = which ? kColDK : kColDV;
@@ -342,9 +344,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 16; ++e)
             hv[e] = pack_half2(__uint_as_float(g[2 * e]) * mul, __uint_as_float(g[2 * e + 1]) * mul);
           uint4* o4 = reinterpret_cast<uint4*>(out + 32 * h);
+          if (key < p.n) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            o4[e] = make_uint4(hv[4 * e], hv[4 * e + 1], hv[4 * e + 2], hv[4 * e + 3]);
+            for (int e = 0; e < 4; ++e)
+              o4[e] = make_uint4(hv[4 * e], hv[4 * e + 1], hv[4 * e + 2], hv[4 * e + 3]);
+          }
         }
       }
     }
