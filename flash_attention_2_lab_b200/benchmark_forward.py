@@ -132,6 +132,9 @@ def main(argv=None) -> None:
                     help="kernel names: sm100 (this library), sdpa (PyTorch, for context)")
     ap.add_argument("--gpus", type=int, default=1, help="devices to split (b, h) over")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--backward", action="store_true",
+                    help="time the backward pass (sm100: fa_bwd_sm100 on saved (o, lse); sdpa: "
+                         "autograd of its forward); TFLOPS = 2.5 x the forward's FLOPs")
     ap.add_argument("--sustained", type=float, default=0.0,
                     help="seconds of back-to-back calls per kernel with clock/power sampling")
     args = ap.parse_args(argv)
@@ -164,8 +167,27 @@ def main(argv=None) -> None:
     print(f"{'kernel':10s} {'median ms':>10s} {'p10 ms':>9s} {'p90 ms':>9s} {'TFLOPS':>9s} "
           f"{'% peak':>7s}")
     results = {}
+    if args.backward:
+        flops *= 2.5  # five GEMMs of the forward's size instead of two
     for name in kernels:
-        if name == "sm100":
+        if name == "sm100" and args.backward:
+            supported = dtype == torch.float16 and args.head_dim == 64 and nk == args.query_length
+
+            def mk(dq, dk, dv):
+                from .autograd import attention_backward, attention_forward_lse
+
+                o, lse = attention_forward_lse(dq, dk, dv, args.causal)
+                do = torch.randn_like(o)
+                return lambda: attention_backward(dq, dk, dv, o, do, lse, args.causal)
+        elif name == "sdpa" and args.backward:
+            supported = True
+
+            def mk(dq, dk, dv):
+                qq, kk, vv = (t.detach().requires_grad_(True) for t in (dq, dk, dv))
+                out = F.scaled_dot_product_attention(qq, kk, vv, is_causal=args.causal)
+                do = torch.randn_like(out)
+                return lambda: torch.autograd.grad(out, (qq, kk, vv), do, retain_graph=True)
+        elif name == "sm100":
             supported = dtype == torch.float16 and args.head_dim == 64
             mk = lambda dq, dk, dv: (lambda: attention_forward(dq, dk, dv, args.causal))
         elif name == "sdpa":
@@ -178,6 +200,16 @@ def main(argv=None) -> None:
             print(f"{name:10s} unsupported for this dtype / head dimension")
             continue
         ops = [(dev, mk(dq, dk, dv)) for dev, dq, dk, dv in shards]
+        if args.backward:
+            # autograd needs grad mode; time the ops outside inference_mode
+            ms = time_on_devices(ops, args.samples, args.iterations, args.warmup)
+            med = statistics.median(ms)
+            tf = flops / (med / 1e3) / 1e12
+            results[name] = med
+            print(f"{name:10s} {med:10.4f} {percentile(ms, 0.1):9.4f} "
+                  f"{percentile(ms, 0.9):9.4f} {tf:9.1f} {100 * tf / (peak * args.gpus):6.1f}%  "
+                  f"(backward)")
+            continue
         if args.sustained > 0:
             with torch.inference_mode():
                 ms, mhz, watts, reasons = sustained(ops, args.sustained)

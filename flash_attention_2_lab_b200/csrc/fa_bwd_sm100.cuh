@@ -12,9 +12,9 @@
 // One block per (batch*head, 128-key tile j); it keeps K_j, V_j, dK_j and dV_j
 // on chip and walks the query tiles i (all of them, or i >= j when causal):
 //
-//   warp 4   TMA producer: K_j, V_j once; per query tile Q_i, dO_i and the
+//   warp 8   TMA producer: K_j, V_j once; per query tile Q_i, dO_i and the
 //            row terms (L * log2 e, D) into a two-slot ring.
-//   warp 5   MMA issuer and TMEM owner.  Per query tile:
+//   warp 9   MMA issuer and TMEM owner.  Per query tile:
 //              S^T  = K_j Q_i^T   (SS, 128 keys x 128 queries)     -> TMEM
 //              dP^T = V_j dO_i^T  (SS)                              -> TMEM
 //            then, once the compute warps have written P^T and dS^T,
@@ -22,12 +22,14 @@
 //              dK  += dS^T Q_i    (TS, dS^T read from TMEM)
 //              dQ_i = dS K_j      (SS; dS^T staged in shared memory is read
 //                                  as an MN-major A operand)
-//   warps 0-3  compute, one thread per TMEM lane: for key row k, the 128
-//            queries of the tile: p = 2^(s c - L log2 e), ds = p (dp - D),
+//   warps 0-7  compute, two warps per TMEM lane quadrant (warp w and w + 4
+//            take query columns 0-63 and 64-127 of the same rows): for key
+//            row k, p = 2^(s c - L log2 e), ds = p (dp - D),
 //            both to fp16 into TMEM (and ds into shared memory); then, with
-//            the lane now a query row, the fp32 dQ_i tile is added into a
-//            global fp32 accumulator with vector reductions (the other key
-//            tiles add theirs).
+//            the lane now a query row, the fp32 dQ_i tile goes to a staging
+//            buffer in shared memory, from which one bulk asynchronous
+//            reduction (TMA unit) adds it into the global fp32 dQ
+//            accumulator (32 KiB, contiguous: the other key tiles add theirs).
 //
 // Tensor memory (512 columns): S^T 0-127 (dQ_i reuses 0-63 once S^T is
 // consumed), dP^T 128-255, P^T 256-319 (fp16 pairs), dS^T 320-383 (fp16
@@ -44,10 +46,11 @@
 namespace fa {
 namespace bwd {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kQSlots = 2;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kComputeWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 
 constexpr uint32_t kSmK = 0;
 constexpr uint32_t kSmV = kSmK + kTileBytes;
@@ -56,7 +59,9 @@ constexpr uint32_t kSmDO = kSmQ + kQSlots * kTileBytes;
 constexpr uint32_t kSmDS = kSmDO + kQSlots * kTileBytes;  // two 64-query halves, 16 KiB each
 constexpr uint32_t kSmVec = kSmDS + 2 * kTileBytes;       // per slot: 128 x (L log2 e, D)
 constexpr uint32_t kVecBytes = 128 * 2 * sizeof(float);
-constexpr uint32_t kSmCtl = kSmVec + kQSlots * kVecBytes;
+constexpr uint32_t kSmDQ = kSmVec + kQSlots * kVecBytes;  // fp32 dQ_i staging, 128 x 64
+constexpr uint32_t kDQBytes = 128 * 64 * sizeof(float);
+constexpr uint32_t kSmCtl = kSmDQ + kDQBytes;
 constexpr uint32_t kSmBytes = kSmCtl + 256 + 1024;  // + alignment slack
 
 constexpr uint32_t kColS = 0, kColDP = 128, kColP = 256, kColDS = 320, kColDV = 384,
@@ -66,6 +71,7 @@ struct Ctl {
   uint64_t kv_full;
   uint64_t q_full[kQSlots], q_empty[kQSlots];
   uint64_t s_full, p_full, dq_full, dq_free;
+  uint64_t dqs_full, dqs_free;  // dQ staging written by the 8 compute warps / read by the reduction
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -97,9 +103,11 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
-__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b),
-               "f"(c), "f"(d)
+// global[dst .. dst + bytes) += shared[src ..), fp32, by the TMA unit
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(src), "r"(bytes)
                : "memory");
 }
 
@@ -131,9 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl->q_empty[s]), 1);
     }
     mbar_init(smem_u32(&ctl->s_full), 1);
-    mbar_init(smem_u32(&ctl->p_full), 4);
+    mbar_init(smem_u32(&ctl->p_full), kComputeWarps);
     mbar_init(smem_u32(&ctl->dq_full), 1);
-    mbar_init(smem_u32(&ctl->dq_free), 4);
+    mbar_init(smem_u32(&ctl->dq_free), kComputeWarps);
+    mbar_init(smem_u32(&ctl->dqs_full), kComputeWarps);
+    mbar_init(smem_u32(&ctl->dqs_free), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
     fence_mbar_init();
@@ -244,8 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ compute
-    const int r = warp * 32 + lane;  // TMEM lane: key row, then query row of dQ
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int quad = warp % 4, half = warp / 4;  // lane quadrant, query-column half
+    const int r = quad * 32 + lane;  // TMEM lane: key row, then query row of dQ
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t t_s = tmem + lane_base + kColS, t_dp = tmem + lane_base + kColDP;
     const uint32_t t_p = tmem + lane_base + kColP, t_ds = tmem + lane_base + kColDS;
     const int key = j * 128 + r;
@@ -265,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q_lo = p.causal ? key : 0;  // first query that sees this key
       const bool key_ok = key < p.n;
 #pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
+      for (int ch = 2 * half; ch < 2 * half + 2; ++ch) {
         uint32_t sr[32], dpr[32];
         tmem_ld32(t_s + 32 * ch, sr);
         tmem_ld32(t_dp + 32 * ch, dpr);
@@ -307,30 +318,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- dQ_i (lane = query row) into the fp32 accumulator
       if (!wait(smem_u32(&ctl->dq_full), it & 1)) { ok = false; break; }
       tc_fence_after();
-      const int q = i * 128 + r;
-      float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.n_pad + q) * 64;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t dq[32];
-        tmem_ld32(t_s + 32 * h, dq);
-        tc_wait_ld32(dq);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          red_add_v4(dst + 32 * h + 4 * e, __uint_as_float(dq[4 * e]),
-                     __uint_as_float(dq[4 * e + 1]), __uint_as_float(dq[4 * e + 2]),
-                     __uint_as_float(dq[4 * e + 3]));
-      }
+      uint32_t dq[32];
+      tmem_ld32(t_s + 32 * half, dq);  // this warp's 32 of the 64 dQ columns
+      tc_wait_ld32(dq);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));  // TMEM columns free for S^T
+      // the staging buffer is rewritten once the previous reduction has read it
+      const bool issuer = warp == 0;
+      if (it > 0) {
+        if (issuer && lane == 0) {
+          bulk_wait_group_read0();
+          mbar_arrive(smem_u32(&ctl->dqs_free));
+        }
+        if (!wait(smem_u32(&ctl->dqs_free), (it - 1) & 1)) { ok = false; break; }
+      }
+      // row r: 64 floats = 16 chunks of 16 B; this warp writes chunks 8 half ..
+      // 8 half + 7, starting at a lane-dependent chunk (no bank conflicts)
+      const uint32_t srow = base + kSmDQ + r * 256 + half * 128;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int cc = (e + lane) & 7;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(srow + cc * 16),
+                     "r"(dq[4 * cc]), "r"(dq[4 * cc + 1]), "r"(dq[4 * cc + 2]), "r"(dq[4 * cc + 3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->dqs_full));
+      if (issuer) {
+        if (!wait(smem_u32(&ctl->dqs_full), it & 1)) { ok = false; break; }
+        if (lane == 0) {
+          bulk_reduce_add_f32(p.dq_acc + (static_cast<size_t>(bh) * p.n_pad + i * 128) * 64,
+                              base + kSmDQ, kDQBytes);
+          bulk_commit_group();
+        }
+        __syncwarp();
+      }
     }
+    // the dQ reductions this block issued finish reading the staging buffer
+    // (and land) before the block exits
+    if (warp == 0 && lane == 0) bulk_wait_group0();
+    __syncwarp();
     // ---- dK_j, dV_j (lane = key row): after the last dQ, every MMA is done.
     // The TMEM loads are warp-collective: every lane takes part, only the
     // lanes of keys below n store.
     if (ok) {
       const size_t row = static_cast<size_t>(bh) * p.n + (key < p.n ? key : 0);
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
+      {
+        const int which = half;  // half 0 writes dV, half 1 dK
         const uint32_t col = which ? kColDK : kColDV;
         const float mul = which ? p.scale : 1.f;
         __half* out = (which ? p.dk : p.dv) + row * 64;

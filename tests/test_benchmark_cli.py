@@ -26,3 +26,12 @@ def test_cli_sustained_mode(capsys):
                             "--kernels", "sm100", "--sustained", "1"])
     out = capsys.readouterr().out
     assert "sustained" in out and "TFLOPS/GHz" in out
+
+
+@pytest.mark.gpu
+def test_cli_backward_mode(capsys):
+    benchmark_forward.main(["--batch", "1", "--heads", "4", "--query-length", "512", "--causal",
+                            "--samples", "2", "--iterations", "2", "--warmup", "2",
+                            "--kernels", "sm100", "sdpa", "--backward"])
+    out = capsys.readouterr().out
+    assert "(backward)" in out and "sm100" in out
