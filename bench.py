@@ -403,6 +403,34 @@ def single_gpu_extras(dev, stream, fwd):
             "parity": {"ok": worst <= 1.0, "max_abs": round(max_abs, 6),
                        "worst_err_over_bound": round(worst, 4), "slices": [0, 31]}}
     del q5, k5, v5
+    # Backward (training) on C3, both masks: fa_bwd_sm100 on the saved (o, lse),
+    # and SDPA's autograd on the same inputs as context; TFLOPS counts the
+    # five GEMMs (2.5 x the forward's FLOPs).
+    from flash_attention_2_lab_b200.autograd import attention_backward, attention_forward_lse
+
+    q3, k3, v3 = workloads.make_inputs("c3", seed=0, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    do = torch.randn(q3.shape, device=dev, generator=g).half()
+    for c in (False, True):
+        o, lse = attention_forward_lse(q3, k3, v3, c)
+        bwd = lambda: attention_backward(q3, k3, v3, o, do, lse, c)  # noqa: E731
+        for _ in range(2):
+            bwd()
+        torch.cuda.synchronize()
+        t = time_device(bwd, 5, stream) / 5
+        qs, ks, vs = (x.detach().requires_grad_(True) for x in (q3, k3, v3))
+        out = F.scaled_dot_product_attention(qs, ks, vs, is_causal=c)
+        sd = lambda: torch.autograd.grad(out, (qs, ks, vs), do, retain_graph=True)  # noqa: E731
+        for _ in range(2):
+            sd()
+        torch.cuda.synchronize()
+        ts = time_device(sd, 5, stream) / 5
+        fl = 2.5 * flops_of(4, 32, 8192, c)
+        extra["c3_backward_causal" if c else "c3_backward_noncausal"] = {
+            "ms": round(t, 4), "tflops": round(fl / (t / 1e3) / 1e12, 1),
+            "sdpa_ms": round(ts, 4), "sdpa_tflops": round(fl / (ts / 1e3) / 1e12, 1)}
+        del o, lse, out, qs, ks, vs
+    del q3, k3, v3, do
     return extra
 
 
