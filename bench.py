@@ -270,10 +270,16 @@ def bind_to_cpus(cpus):
         return 0
 
 
-def host_link_ceiling(dev, world, local, nbytes=1 << 30, reps=3):
+def host_link_ceiling(dev, world, local, d2h_share=1.0, nbytes=1 << 30, reps=3,
+                      chunk_up=0, chunk_down=0, chunks=0):
     """Concurrent plain pinned copies on every rank at once: host->device,
-    device->host, and both directions together (as the e2e pipeline runs
-    them).  Returns the whole-job GB/s of each (bytes of all ranks / max time)."""
+    device->host, both directions with equal bytes, and both directions with
+    the e2e step's own mix (``d2h_share`` bytes device->host per byte
+    host->device).  With ``chunks`` > 0 also "pipe": the e2e step's copy
+    schedule without its kernels (``chunks`` rounds of ``chunk_up`` bytes up
+    on one stream and ``chunk_down`` bytes down on another).  Returns the
+    whole-job GB/s of each (bytes of all ranks / the max-over-ranks time of
+    the best repetition)."""
     import torch
     import torch.distributed as dist
 
@@ -282,6 +288,7 @@ def host_link_ceiling(dev, world, local, nbytes=1 << 30, reps=3):
     devb = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     devb2 = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    mix_d2h = max(16, (int(nbytes * min(d2h_share, 1.0)) // 16) * 16)
 
     def barrier():
         torch.cuda.synchronize()
@@ -289,24 +296,38 @@ def host_link_ceiling(dev, world, local, nbytes=1 << 30, reps=3):
             dist.barrier(device_ids=[local])
 
     def timed(kind):
-        best = float("inf")
+        up = nbytes if kind in ("h2d", "both", "mix") else 0
+        down = {"d2h": nbytes, "both": nbytes, "mix": mix_d2h}.get(kind, 0)
+        times = []
         for _ in range(reps):
             barrier()
             t0 = time.perf_counter()
-            if kind in ("h2d", "both"):
+            if up:
                 with torch.cuda.stream(s1):
-                    devb.copy_(host, non_blocking=True)
-            if kind in ("d2h", "both"):
+                    devb[:up].copy_(host[:up], non_blocking=True)
+            if down:
                 with torch.cuda.stream(s2):
-                    host2.copy_(devb2, non_blocking=True)
+                    host2[:down].copy_(devb2[:down], non_blocking=True)
             s1.synchronize()
             s2.synchronize()
-            best = min(best, time.perf_counter() - t0)
-        t = max_over_ranks_vec([best], dev)[0]
-        moved = nbytes * (2 if kind == "both" else 1) * world
-        return moved / t / 1e9
+            times.append(max_over_ranks_vec([time.perf_counter() - t0], dev)[0])
+        return (up + down) * world / min(times) / 1e9
 
-    out = {k: round(timed(k), 2) for k in ("h2d", "d2h", "both")}
+    out = {k: round(timed(k), 2) for k in ("h2d", "d2h", "both", "mix")}
+    if chunks > 0 and chunk_up <= nbytes and chunk_down <= nbytes:
+        times = []
+        for _ in range(reps):
+            barrier()
+            t0 = time.perf_counter()
+            for _ in range(chunks):
+                with torch.cuda.stream(s1):
+                    devb[:chunk_up].copy_(host[:chunk_up], non_blocking=True)
+                with torch.cuda.stream(s2):
+                    host2[:chunk_down].copy_(devb2[:chunk_down], non_blocking=True)
+            s1.synchronize()
+            s2.synchronize()
+            times.append(max_over_ranks_vec([time.perf_counter() - t0], dev)[0])
+        out["pipe"] = round((chunk_up + chunk_down) * chunks * world / min(times) / 1e9, 2)
     del host, host2, devb, devb2
     return out
 
@@ -529,13 +550,15 @@ def run_ours(args):
     h2d = int(sum_over_ranks(sum(t.numel() * t.element_size() for t in (hq, hk, hv)), dev))
     d2h = int(sum_over_ranks(hout.numel() * hout.element_size(), dev))
     del hq, hk, hv, hout
-    link = host_link_ceiling(dev, world, local)
+    per_b = q[0].numel() * q.element_size()  # one batch element of one tensor
+    link = host_link_ceiling(dev, world, local, d2h_share=d2h / max(h2d, 1),
+                             chunk_up=3 * per_b, chunk_down=per_b, chunks=len(mine))
     e2e_gbs = (h2d + d2h) / (e2e_ms / 1e3) / 1e9
     # The host-link bound of one step: the copies alone at the concurrent
     # ceilings (each direction on its own, and both together), whichever is
     # slowest; the kernel itself is far shorter than any of them.
     link_ms = max(h2d / (link["h2d"] * 1e9), d2h / (link["d2h"] * 1e9),
-                  (h2d + d2h) / (link["both"] * 1e9)) * 1e3
+                  (h2d + d2h) / (max(link["mix"], link.get("pipe", 0.0)) * 1e9)) * 1e3
     nodes = max_over_ranks_vec([numa], dev)  # all ranks' nodes agree here or the max shows one
 
     extra = {}
@@ -584,11 +607,14 @@ def run_ours(args):
                 "api": "flash_attention_2_lab_b200.host_pipeline.attention_forward_host",
                 "host_gbs": round(e2e_gbs, 2),
                 "h2d_ceiling_gbs": link["h2d"], "d2h_ceiling_gbs": link["d2h"],
-                "bidir_ceiling_gbs": link["both"],
+                "bidir_ceiling_gbs": link["both"], "mixed_ceiling_gbs": link["mix"],
+                "pipeline_copy_ceiling_gbs": link.get("pipe"),
                 "frac_of_bidir_ceiling": round(e2e_gbs / link["both"], 4),
                 "link_bound_ms": round(link_ms, 3),
                 "frac_of_link_bound": round(link_ms / e2e_ms, 4),
-                "ceiling": "plain 1 GiB pinned copies on all ranks at once, max-over-ranks time",
+                "ceiling": "pinned copies on all ranks at once, max-over-ranks time: 1 GiB up / "
+                           "down / both, the e2e byte mix, and the e2e copy schedule without "
+                           "kernels (pipeline); the bound uses the faster of the last two",
                 "numa_node": int(nodes[0]), "bound_cpus": bound_cpus},
         "gpu_launches": args.steps,
         "clocks": clocks,
