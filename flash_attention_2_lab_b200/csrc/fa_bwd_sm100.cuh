@@ -14,6 +14,9 @@
 //
 //   warp 8   TMA producer: K_j, V_j once; per query tile Q_i, dO_i and the
 //            row terms (L * log2 e, D) into a two-slot ring.
+//   warp 10  issues one bulk asynchronous reduction per query tile (dQ_i
+//            staging -> global fp32 accumulator) and frees the staging buffer
+//            once the reduction has read it, off the compute warps' path.
 //   warp 9   MMA issuer and TMEM owner.  Per query tile:
 //              S^T  = K_j Q_i^T   (SS, 128 keys x 128 queries)     -> TMEM
 //              dP^T = V_j dO_i^T  (SS)                              -> TMEM
@@ -29,7 +32,9 @@
 //            the lane now a query row, the fp32 dQ_i tile goes to a staging
 //            buffer in shared memory, from which one bulk asynchronous
 //            reduction (TMA unit) adds it into the global fp32 dQ
-//            accumulator (32 KiB, contiguous: the other key tiles add theirs).
+//            accumulator (32 KiB, contiguous: the other key tiles add theirs;
+//            the 16-byte chunks of each half-row sit XOR-swizzled by the row,
+//            which dq_convert_kernel undoes).
 //
 // Tensor memory (512 columns): S^T 0-127 (dQ_i reuses 0-63 once S^T is
 // consumed), dP^T 128-255, P^T 256-319 (fp16 pairs), dS^T 320-383 (fp16
@@ -46,11 +51,12 @@
 namespace fa {
 namespace bwd {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kQSlots = 2;
 constexpr int kComputeWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kReduceWarp = 10;  // issues the bulk dQ reductions
 
 constexpr uint32_t kSmK = 0;
 constexpr uint32_t kSmV = kSmK + kTileBytes;
@@ -131,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int i0 = first_qtile(p, j);
   const int n_steps = p.n_kt - i0;
   volatile int* abort_flag = &ctl->abort;
+  auto qtile = [&](int it) { return i0 + it; };
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&ctl->kv_full), 1);
@@ -252,6 +259,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(smem_u32(&ctl->drain), 0, nullptr, p.status, kStatusTimeoutDrain, kDrainLimitNs);
     }
     __syncwarp();
+  } else if (warp == kReduceWarp) {
+    // ------------------------------------------------------------ dQ reductions
+    for (int it = 0; it < n_steps; ++it) {
+      if (!mbar_wait_warp(smem_u32(&ctl->dqs_full), it & 1, abort_flag, p.status,
+                          kStatusTimeoutSoftmax, p.limit_ns))
+        break;
+      if (lane == 0) {
+        bulk_reduce_add_f32(p.dq_acc + (static_cast<size_t>(bh) * p.n_pad + qtile(it) * 128) * 64,
+                            base + kSmDQ, kDQBytes);
+        bulk_commit_group();
+        bulk_wait_group_read0();  // the staging buffer has been read
+        mbar_arrive(smem_u32(&ctl->dqs_free));
+      }
+      __syncwarp();
+    }
+    // every reduction lands before the block exits
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ compute
     const int quad = warp % 4, half = warp / 4;  // lane quadrant, query-column half
@@ -325,41 +350,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));  // TMEM columns free for S^T
       // the staging buffer is rewritten once the previous reduction has read it
-      const bool issuer = warp == 0;
-      if (it > 0) {
-        if (issuer && lane == 0) {
-          bulk_wait_group_read0();
-          mbar_arrive(smem_u32(&ctl->dqs_free));
-        }
-        if (!wait(smem_u32(&ctl->dqs_free), (it - 1) & 1)) { ok = false; break; }
-      }
-      // row r: 64 floats = 16 chunks of 16 B; this warp writes chunks 8 half ..
-      // 8 half + 7, starting at a lane-dependent chunk (no bank conflicts)
+      if (it > 0 && !wait(smem_u32(&ctl->dqs_free), (it - 1) & 1)) { ok = false; break; }
+      // row r: 64 floats = 16 chunks of 16 B; this warp owns chunks 8 half ..
+      // 8 half + 7 and stores chunk c at position c ^ (r & 7) of its half (the
+      // accumulator keeps that order; eight consecutive rows hit eight
+      // different bank groups)
       const uint32_t srow = base + kSmDQ + r * 256 + half * 128;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int cc = (e + lane) & 7;
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(srow + cc * 16),
-                     "r"(dq[4 * cc]), "r"(dq[4 * cc + 1]), "r"(dq[4 * cc + 2]), "r"(dq[4 * cc + 3])
+      for (int e = 0; e < 8; ++e)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(srow + ((e ^ (r & 7)) << 4)),
+                     "r"(dq[4 * e]), "r"(dq[4 * e + 1]), "r"(dq[4 * e + 2]), "r"(dq[4 * e + 3])
                      : "memory");
-      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctl->dqs_full));
-      if (issuer) {
-        if (!wait(smem_u32(&ctl->dqs_full), it & 1)) { ok = false; break; }
-        if (lane == 0) {
-          bulk_reduce_add_f32(p.dq_acc + (static_cast<size_t>(bh) * p.n_pad + i * 128) * 64,
-                              base + kSmDQ, kDQBytes);
-          bulk_commit_group();
-        }
-        __syncwarp();
-      }
     }
-    // the dQ reductions this block issued finish reading the staging buffer
-    // (and land) before the block exits
-    if (warp == 0 && lane == 0) bulk_wait_group0();
-    __syncwarp();
     // ---- dK_j, dV_j (lane = key row): after the last dQ, every MMA is done.
     // The TMEM loads are warp-collective: every lane takes part, only the
     // lanes of keys below n store.
@@ -438,9 +443,10 @@ __global__ void dq_convert_kernel(const float* __restrict__ dq_acc, __half* __re
   const int g = static_cast<int>(idx % 8);
   const int64_t bh = row / n;
   const int q = static_cast<int>(row - bh * n);
-  const float4* src =
-      reinterpret_cast<const float4*>(dq_acc + (static_cast<size_t>(bh) * n_pad + q) * 64 + 8 * g);
-  const float4 a = src[0], b = src[1];
+  // chunk c (4 floats) of a 32-float half sits at position c ^ (q & 7)
+  const float4* src = reinterpret_cast<const float4*>(dq_acc + (static_cast<size_t>(bh) * n_pad + q) * 64);
+  const int c0 = 2 * g, hb = c0 & 8, sw = q & 7;
+  const float4 a = src[hb | ((c0 & 7) ^ sw)], b = src[hb | (((c0 + 1) & 7) ^ sw)];
   uint4 out;
   out.x = pack_half2(a.x * scale, a.y * scale);
   out.y = pack_half2(a.z * scale, a.w * scale);
