@@ -21,14 +21,17 @@
 //              S^T  = K_j Q_i^T   (SS, 128 keys x 128 queries)     -> TMEM
 //              dP^T = V_j dO_i^T  (SS)                              -> TMEM
 //            then, once the compute warps have written P^T and dS^T,
+//              S^T of tile i+1 (its exponentials overlap the three below)
 //              dV  += P^T  dO_i   (TS, P^T read from TMEM)
 //              dK  += dS^T Q_i    (TS, dS^T read from TMEM)
 //              dQ_i = dS K_j      (SS; dS^T staged in shared memory is read
-//                                  as an MN-major A operand)
+//                                  as an MN-major A operand) -> dP^T columns
+//            and dP^T of tile i+1 once dQ_i has been read.
 //   warps 0-7  compute, two warps per TMEM lane quadrant (warp w and w + 4
 //            take query columns 0-63 and 64-127 of the same rows): for key
-//            row k, p = 2^(s c - L log2 e), ds = p (dp - D),
-//            both to fp16 into TMEM (and ds into shared memory); then, with
+//            row k, p = 2^(s c - L log2 e) (kept in registers as fp16 until
+//            the previous tile's dV MMA is done), ds = p (dp - D) with that
+//            fp16 p, both into TMEM (and ds into shared memory); then, with
 //            the lane now a query row, the fp32 dQ_i tile goes to a staging
 //            buffer in shared memory, from which one bulk asynchronous
 //            reduction (TMA unit) adds it into the global fp32 dQ
@@ -36,8 +39,8 @@
 //            the 16-byte chunks of each half-row sit XOR-swizzled by the row,
 //            which dq_convert_kernel undoes).
 //
-// Tensor memory (512 columns): S^T 0-127 (dQ_i reuses 0-63 once S^T is
-// consumed), dP^T 128-255, P^T 256-319 (fp16 pairs), dS^T 320-383 (fp16
+// Tensor memory (512 columns): S^T 0-127, dP^T 128-255 (dQ_i reuses 128-191
+// once dP^T is consumed), P^T 256-319 (fp16 pairs), dS^T 320-383 (fp16
 // pairs), dV 384-447, dK 448-511.
 //
 // Shared-memory descriptors of MN-major operands (128-byte swizzle): an atom
@@ -47,6 +50,8 @@
 //
 // Every wait is bounded, as in the forward kernel.
 #pragma once
+
+#include <type_traits>
 
 namespace fa {
 namespace bwd {
@@ -63,7 +68,7 @@ constexpr uint32_t kSmV = kSmK + kTileBytes;
 constexpr uint32_t kSmQ = kSmV + kTileBytes;
 constexpr uint32_t kSmDO = kSmQ + kQSlots * kTileBytes;
 constexpr uint32_t kSmDS = kSmDO + kQSlots * kTileBytes;  // two 64-query halves, 16 KiB each
-constexpr uint32_t kSmVec = kSmDS + 2 * kTileBytes;       // per slot: 128 x (L log2 e, D)
+constexpr uint32_t kSmVec = kSmDS + 2 * kTileBytes;       // per slot: 128 L log2 e, 128 D
 constexpr uint32_t kVecBytes = 128 * 2 * sizeof(float);
 constexpr uint32_t kSmDQ = kSmVec + kQSlots * kVecBytes;  // fp32 dQ_i staging, 128 x 64
 constexpr uint32_t kDQBytes = 128 * 64 * sizeof(float);
@@ -76,7 +81,7 @@ constexpr uint32_t kColS = 0, kColDP = 128, kColP = 256, kColDS = 320, kColDV = 
 struct Ctl {
   uint64_t kv_full;
   uint64_t q_full[kQSlots], q_empty[kQSlots];
-  uint64_t s_full, p_full, dq_full, dq_free;
+  uint64_t s_full, dp_full, p_full, dq_full, dq_free;
   uint64_t dqs_full, dqs_free;  // dQ staging written by the 8 compute warps / read by the reduction
   uint64_t drain;
   uint32_t tmem_base;
@@ -92,7 +97,7 @@ struct Params {
   int n_kt;          // key (and query) tiles per (batch, head)
   float scale;       // softmax scale
   float scale_log2;  // scale * log2(e)
-  const float2* rowterm;  // [bh][n_pad]: (L log2 e, D)
+  const float* rowterm;   // [bh][n_pad / 128][2][128]: per query tile L log2 e, then D
   float* dq_acc;          // [bh][n_pad][64] fp32, zeroed before the launch
   __half* dk;             // [bh][n][64]
   __half* dv;
@@ -146,6 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl->q_empty[s]), 1);
     }
     mbar_init(smem_u32(&ctl->s_full), 1);
+    mbar_init(smem_u32(&ctl->dp_full), 1);
     mbar_init(smem_u32(&ctl->p_full), kComputeWarps);
     mbar_init(smem_u32(&ctl->dq_full), 1);
     mbar_init(smem_u32(&ctl->dq_free), kComputeWarps);
@@ -189,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(base + kSmQ + slot * kTileBytes, &tm_q, full, 0, i * 128, bh);
         tma_load_3d(base + kSmDO + slot * kTileBytes, &tm_do, full, 0, i * 128, bh);
         bulk_load(base + kSmVec + slot * kVecBytes,
-                  p.rowterm + static_cast<size_t>(bh) * p.n_pad + i * 128, kVecBytes, full);
+                  p.rowterm + (static_cast<size_t>(bh) * p.n_pad + i * 128) * 2, kVecBytes, full);
       }
       __syncwarp();
       issued = it + 1;
@@ -216,27 +222,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wait = [&](uint32_t bar, uint32_t parity) {
       return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutMma, p.limit_ns);
     };
-    bool ok = wait(smem_u32(&ctl->kv_full), 0);
-    for (int it = 0; ok && it < n_steps; ++it) {
-      const int slot = it % kQSlots;
-      if (!wait(smem_u32(&ctl->q_full[slot]), (it / kQSlots) & 1)) break;
-      // S^T is written over the previous dQ tile: it must have been read
-      if (it > 0 && !wait(smem_u32(&ctl->dq_free), (it - 1) & 1)) break;
-      tc_fence_after();
-      const uint64_t dq_ = smem_desc_sw128(base + kSmQ, 16, 1024) + slot * kTileDesc;
-      const uint64_t ddo = smem_desc_sw128(base + kSmDO, 16, 1024) + slot * kTileDesc;
+    const uint64_t dq0 = smem_desc_sw128(base + kSmQ, 16, 1024);
+    const uint64_t ddo0 = smem_desc_sw128(base + kSmDO, 16, 1024);
+    auto issue_s = [&](int it) {  // S^T = K_j Q_i^T
+      const uint64_t dq_ = dq0 + (it % kQSlots) * kTileDesc;
       if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_ss_f16(tmem + kColS, dk_ + 2 * kk, dq_ + 2 * kk, idesc_s, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ss_f16(tmem + kColDP, dv_ + 2 * kk, ddo + 2 * kk, idesc_s, kk > 0);
         tc_commit(smem_u32(&ctl->s_full));
       }
       __syncwarp();
-      if (!wait(smem_u32(&ctl->p_full), it & 1)) break;
+    };
+    auto issue_dp = [&](int it) {  // dP^T = V_j dO_i^T
+      const uint64_t ddo = ddo0 + (it % kQSlots) * kTileDesc;
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss_f16(tmem + kColDP, dv_ + 2 * kk, ddo + 2 * kk, idesc_s, kk > 0);
+        tc_commit(smem_u32(&ctl->dp_full));
+      }
+      __syncwarp();
+    };
+    bool ok = wait(smem_u32(&ctl->kv_full), 0) && n_steps > 0 && wait(smem_u32(&ctl->q_full[0]), 0);
+    if (ok) {
       tc_fence_after();
+      issue_s(0);
+      issue_dp(0);
+    }
+    for (int it = 0; ok && it < n_steps; ++it) {
+      const int slot = it % kQSlots;
+      // P^T, dS^T written; S^T and dP^T of this tile read
+      if (!wait(smem_u32(&ctl->p_full), it & 1)) break;
+      if (it + 1 < n_steps) {
+        if (!wait(smem_u32(&ctl->q_full[(it + 1) % kQSlots]), ((it + 1) / kQSlots) & 1)) break;
+        tc_fence_after();
+        issue_s(it + 1);
+      }
+      tc_fence_after();
+      const uint64_t dq_ = dq0 + slot * kTileDesc;
+      const uint64_t ddo = ddo0 + slot * kTileDesc;
       if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // 16 queries per step
@@ -248,11 +273,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                      (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // 16 keys per step
-          mma_ss_f16(tmem + kColS, dds + 128 * kk, dk_ + 128 * kk, idesc_dq, kk > 0);
+          mma_ss_f16(tmem + kColDP, dds + 128 * kk, dk_ + 128 * kk, idesc_dq, kk > 0);
         tc_commit(smem_u32(&ctl->dq_full));
         tc_commit(smem_u32(&ctl->q_empty[slot]));
       }
       __syncwarp();
+      if (it + 1 < n_steps) {
+        // dP^T of the next tile goes over dQ_i: wait until it has been read
+        if (!wait(smem_u32(&ctl->dq_free), it & 1)) break;
+        tc_fence_after();
+        issue_dp(it + 1);
+      }
     }
     if (lane == 0) {
       tc_commit(smem_u32(&ctl->drain));
@@ -283,6 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quad * 32 + lane;  // TMEM lane: key row, then query row of dQ
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t t_s = tmem + lane_base + kColS, t_dp = tmem + lane_base + kColDP;
+    const uint32_t t_dq = t_dp;  // dQ_i is written over dP^T
     const uint32_t t_p = tmem + lane_base + kColP, t_ds = tmem + lane_base + kColDS;
     const int key = j * 128 + r;
     const float c = p.scale_log2;
@@ -290,38 +322,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax,
                             p.limit_ns);
     };
-    bool ok = true;
-    for (int it = 0; it < n_steps; ++it) {
+    // keys past n and (causal) queries before this key contribute nothing
+    const int q_lo = p.causal ? key : 0;  // first query that sees this key
+    const bool key_ok = key < p.n;
+    const int key_max = j * 128 + quad * 32 + 31;  // last key of this warp
+    // p of this warp's 64 queries of tile it, fp16 pairs: pk[16 c + u / 2]
+    // holds queries 32 (2 half + c) + u, + 1
+    uint32_t pk[32];
+    // exponentials of tile it from S^T (needs S^T and the row terms of tile it)
+    auto phase_p = [&](int it) -> bool {
       const int i = i0 + it, slot = it % kQSlots;
-      if (!wait(smem_u32(&ctl->q_full[slot]), (it / kQSlots) & 1)) { ok = false; break; }
-      if (!wait(smem_u32(&ctl->s_full), it & 1)) { ok = false; break; }
+      if (!wait(smem_u32(&ctl->q_full[slot]), (it / kQSlots) & 1)) return false;
+      if (!wait(smem_u32(&ctl->s_full), it & 1)) return false;
       tc_fence_after();
-      const float2* rt = reinterpret_cast<const float2*>(gen_base + kSmVec + slot * kVecBytes);
-      // keys past n and (causal) queries before this key contribute nothing
-      const int q_lo = p.causal ? key : 0;  // first query that sees this key
-      const bool key_ok = key < p.n;
-#pragma unroll 1
-      for (int ch = 2 * half; ch < 2 * half + 2; ++ch) {
-        uint32_t sr[32], dpr[32];
-        tmem_ld32(t_s + 32 * ch, sr);
-        tmem_ld32(t_dp + 32 * ch, dpr);
-        tc_wait_ld();
-        uint32_t pk[16], dk16[16];
+      const float* l2 = reinterpret_cast<const float*>(gen_base + kSmVec + slot * kVecBytes);
+      // masks only where this warp's 32 keys x 64 queries reach past n or
+      // (causal) below the diagonal
+      const int q_min = i * 128 + 64 * half;
+      const bool masked = key_max >= p.n || q_min + 63 >= p.n || (p.causal && q_min < key_max);
+      auto exps = [&](auto mask_tag) {
+        constexpr bool kMask = decltype(mask_tag)::value;
 #pragma unroll
-        for (int u = 0; u < 32; u += 2) {
-          const int ql = 32 * ch + u;  // query within the tile
-          const float4 t2 = *reinterpret_cast<const float4*>(rt + ql);  // (L2, D) of ql, ql+1
-          const int q = i * 128 + ql;
-          float p0 = ex2_approx(__uint_as_float(sr[u]) * c - t2.x);
-          float p1 = ex2_approx(__uint_as_float(sr[u + 1]) * c - t2.z);
-          if (!key_ok || q < q_lo || q >= p.n) p0 = 0.f;
-          if (!key_ok || q + 1 < q_lo || q + 1 >= p.n) p1 = 0.f;
-          const float d0 = p0 * (__uint_as_float(dpr[u]) - t2.y);
-          const float d1 = p1 * (__uint_as_float(dpr[u + 1]) - t2.w);
-          pk[u / 2] = pack_half2(p0, p1);
-          dk16[u / 2] = pack_half2(d0, d1);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int ch = 2 * half + c2;
+          uint32_t sr[32];
+          tmem_ld32(t_s + 32 * ch, sr);
+          tc_wait_ld32(sr);
+#pragma unroll
+          for (int u = 0; u < 32; u += 4) {
+            const int ql = 32 * ch + u;  // query within the tile
+            const float4 lv = *reinterpret_cast<const float4*>(l2 + ql);
+            const float lq[4] = {lv.x, lv.y, lv.z, lv.w};
+            float pv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              pv[e] = ex2_approx(__uint_as_float(sr[u + e]) * c - lq[e]);
+              if (kMask) {
+                const int q = i * 128 + ql + e;
+                if (!key_ok || q < q_lo || q >= p.n) pv[e] = 0.f;
+              }
+            }
+            pk[16 * c2 + u / 2] = pack_half2(pv[0], pv[1]);
+            pk[16 * c2 + u / 2 + 1] = pack_half2(pv[2], pv[3]);
+          }
         }
-        tmem_st16(t_p + 16 * ch, pk);
+      };
+      if (masked)
+        exps(std::true_type{});
+      else
+        exps(std::false_type{});
+      return true;
+    };
+    bool ok = phase_p(0);
+    for (int it = 0; ok && it < n_steps; ++it) {
+      const int slot = it % kQSlots;
+      // P^T of tile it into TMEM: the previous tile's dV MMA (which read the
+      // columns) completed before its dQ was signalled
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) tmem_st16(t_p + 16 * (2 * half + c2), pk + 16 * c2);
+      if (!wait(smem_u32(&ctl->dp_full), it & 1)) { ok = false; break; }
+      tc_fence_after();
+      const float* dvec =
+          reinterpret_cast<const float*>(gen_base + kSmVec + slot * kVecBytes) + 128;
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) {
+        const int ch = 2 * half + c2;
+        uint32_t dpr[32];
+        tmem_ld32(t_dp + 32 * ch, dpr);
+        tc_wait_ld32(dpr);
+        uint32_t dk16[16];
+#pragma unroll
+        for (int u = 0; u < 32; u += 4) {
+          const float4 dv4 = *reinterpret_cast<const float4*>(dvec + 32 * ch + u);  // D
+          const float2 pa = __half22float2(*reinterpret_cast<const __half2*>(&pk[16 * c2 + u / 2]));
+          const float2 pb =
+              __half22float2(*reinterpret_cast<const __half2*>(&pk[16 * c2 + u / 2 + 1]));
+          dk16[u / 2] = pack_half2(pa.x * (__uint_as_float(dpr[u]) - dv4.x),
+                                   pa.y * (__uint_as_float(dpr[u + 1]) - dv4.y));
+          dk16[u / 2 + 1] = pack_half2(pb.x * (__uint_as_float(dpr[u + 2]) - dv4.z),
+                                       pb.y * (__uint_as_float(dpr[u + 3]) - dv4.w));
+        }
         tmem_st16(t_ds + 16 * ch, dk16);
         // dS^T row r, queries 32 ch .. 32 ch + 31: half ch / 2 of the staged
         // tile, four 16-byte chunks of its 128-byte row (128B swizzle)
@@ -340,15 +420,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctl->p_full));
+      // ---- exponentials of the next tile while the tensor cores run this one's
+      // dV, dK, dQ
+      if (it + 1 < n_steps && !phase_p(it + 1)) { ok = false; break; }
       // ---- dQ_i (lane = query row) into the fp32 accumulator
       if (!wait(smem_u32(&ctl->dq_full), it & 1)) { ok = false; break; }
       tc_fence_after();
       uint32_t dq[32];
-      tmem_ld32(t_s + 32 * half, dq);  // this warp's 32 of the 64 dQ columns
+      tmem_ld32(t_dq + 32 * half, dq);  // this warp's 32 of the 64 dQ columns
       tc_wait_ld32(dq);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));  // TMEM columns free for S^T
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));  // TMEM columns free for dP^T
       // the staging buffer is rewritten once the previous reduction has read it
       if (it > 0 && !wait(smem_u32(&ctl->dqs_free), (it - 1) & 1)) { ok = false; break; }
       // row r: 64 floats = 16 chunks of 16 B; this warp owns chunks 8 half ..
@@ -403,16 +486,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Row terms for the backward: (L log2 e, D = rowsum(dO * O)) per query row,
-// zero for the padding rows up to n_pad.  One thread per row.
+// Row terms for the backward: L log2 e and D = rowsum(dO * O) per query row,
+// zero for the padding rows up to n_pad, stored per 128-query tile as 128 L
+// values then 128 D values.  One thread per row.
 __global__ void rowterm_kernel(const __half* __restrict__ o, const __half* __restrict__ d_o,
-                               const float* __restrict__ lse, float2* __restrict__ rowterm,
+                               const float* __restrict__ lse, float* __restrict__ rowterm,
                                int n, int n_pad, int64_t rows_pad) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= rows_pad) return;
   const int64_t bh = idx / n_pad;
   const int q = static_cast<int>(idx - bh * n_pad);
-  float2 out = make_float2(0.f, 0.f);
+  float l2 = 0.f, dsum = 0.f;
   if (q < n) {
     const size_t row = static_cast<size_t>(bh) * n + q;
     const uint4* a = reinterpret_cast<const uint4*>(o + row * 64);
@@ -429,9 +513,13 @@ __global__ void rowterm_kernel(const __half* __restrict__ o, const __half* __res
         acc = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, acc));
       }
     }
-    out = make_float2(lse[row] * 1.4426950408889634f, acc);
+    l2 = lse[row] * 1.4426950408889634f;
+    dsum = acc;
   }
-  rowterm[idx] = out;
+  // tile-blocked: 128 L log2 e, then 128 D, per query tile
+  float* dst = rowterm + (idx - (q & 127)) * 2 + (q & 127);
+  dst[0] = l2;
+  dst[128] = dsum;
 }
 
 // dq = scale * dq_acc, fp32 -> fp16, rows below n.

@@ -1474,13 +1474,13 @@ int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, con
   if (rc != FA_OK) return rc;
 
   // scratch: [counter prefix of the split mode, left alone][row terms][dQ accumulator]
-  const size_t rowterm_bytes = align256(static_cast<size_t>(bh) * n_pad * sizeof(float2));
+  const size_t rowterm_bytes = align256(static_cast<size_t>(bh) * n_pad * 2 * sizeof(float));
   const size_t dq_bytes = static_cast<size_t>(bh) * n_pad * 64 * sizeof(float);
   void* ws = nullptr;
   if ((rc = get_workspace(dev, stream, kCounterBytes + rowterm_bytes + dq_bytes, &ws)) != FA_OK)
     return rc;
   uint8_t* wb = static_cast<uint8_t*>(ws) + kCounterBytes;
-  float2* rowterm = reinterpret_cast<float2*>(wb);
+  float* rowterm = reinterpret_cast<float*>(wb);
   float* dq_acc = reinterpret_cast<float*>(wb + rowterm_bytes);
   e = cudaMemsetAsync(dq_acc, 0, dq_bytes, stream);
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "dQ clear: %s", cudaGetErrorString(e));
