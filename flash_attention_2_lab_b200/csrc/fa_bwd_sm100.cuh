@@ -20,8 +20,9 @@
 //   warp 9   MMA issuer and TMEM owner.  Per query tile:
 //              S^T  = K_j Q_i^T   (SS, 128 keys x 128 queries)     -> TMEM
 //              dP^T = V_j dO_i^T  (SS)                              -> TMEM
-//            then, once the compute warps have written P^T and dS^T,
-//              S^T of tile i+1 (its exponentials overlap the three below)
+//            then S^T of tile i+1 as soon as the exponentials of tile i
+//            have read S^T, and once the compute warps have written P^T and
+//            dS^T (the exponentials of tile i+1 overlap these three):
 //              dV  += P^T  dO_i   (TS, P^T read from TMEM)
 //              dK  += dS^T Q_i    (TS, dS^T read from TMEM)
 //              dQ_i = dS K_j      (SS; dS^T staged in shared memory is read
@@ -81,7 +82,7 @@ constexpr uint32_t kColS = 0, kColDP = 128, kColP = 256, kColDS = 320, kColDV = 
 struct Ctl {
   uint64_t kv_full;
   uint64_t q_full[kQSlots], q_empty[kQSlots];
-  uint64_t s_full, dp_full, p_full, dq_full, dq_free;
+  uint64_t s_full, s_free, dp_full, p_full, dq_full, dq_free;
   uint64_t dqs_full, dqs_free;  // dQ staging written by the 8 compute warps / read by the reduction
   uint64_t drain;
   uint32_t tmem_base;
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(smem_u32(&ctl->s_full), 1);
     mbar_init(smem_u32(&ctl->dp_full), 1);
+    mbar_init(smem_u32(&ctl->s_free), kComputeWarps);
     mbar_init(smem_u32(&ctl->p_full), kComputeWarps);
     mbar_init(smem_u32(&ctl->dq_full), 1);
     mbar_init(smem_u32(&ctl->dq_free), kComputeWarps);
@@ -252,13 +254,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int it = 0; ok && it < n_steps; ++it) {
       const int slot = it % kQSlots;
-      // P^T, dS^T written; S^T and dP^T of this tile read
-      if (!wait(smem_u32(&ctl->p_full), it & 1)) break;
       if (it + 1 < n_steps) {
+        // S^T of the next tile once this tile's exponentials have read S^T
+        if (!wait(smem_u32(&ctl->s_free), it & 1)) break;
         if (!wait(smem_u32(&ctl->q_full[(it + 1) % kQSlots]), ((it + 1) / kQSlots) & 1)) break;
         tc_fence_after();
         issue_s(it + 1);
       }
+      // P^T, dS^T written; dP^T of this tile read
+      if (!wait(smem_u32(&ctl->p_full), it & 1)) break;
       tc_fence_after();
       const uint64_t dq_ = dq0 + slot * kTileDesc;
       const uint64_t ddo = ddo0 + slot * kTileDesc;
@@ -371,6 +375,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         exps(std::true_type{});
       else
         exps(std::false_type{});
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->s_free));  // S^T read: the next one may start
       return true;
     };
     bool ok = phase_p(0);
