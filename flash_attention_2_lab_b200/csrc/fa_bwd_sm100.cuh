@@ -32,13 +32,14 @@
 //            take query columns 0-63 and 64-127 of the same rows): for key
 //            row k, p = 2^(s c - L log2 e) (kept in registers as fp16 until
 //            the previous tile's dV MMA is done), ds = p (dp - D) with that
-//            fp16 p, both into TMEM (and ds into shared memory); then, with
-//            the lane now a query row, the fp32 dQ_i tile goes to a staging
-//            buffer in shared memory, from which one bulk asynchronous
-//            reduction (TMA unit) adds it into the global fp32 dQ
-//            accumulator (32 KiB, contiguous: the other key tiles add theirs;
-//            the 16-byte chunks of each half-row sit XOR-swizzled by the row,
-//            which dq_convert_kernel undoes).
+//            fp16 p, both into TMEM (and ds into shared memory).
+//   warps 11-14 dQ_i readout, one warp per TMEM lane quadrant (lane = query
+//            row): the fp32 dQ_i tile goes to a staging buffer in shared
+//            memory, from which one bulk asynchronous reduction (TMA unit,
+//            issued by warp 10) adds it into the global fp32 dQ accumulator
+//            (32 KiB, contiguous: the other key tiles add theirs; the 16-byte
+//            chunks of each half-row sit XOR-swizzled by the row, which
+//            dq_convert_kernel undoes).
 //
 // Tensor memory (512 columns): S^T 0-127, dP^T 128-255 (dQ_i reuses 128-191
 // once dP^T is consumed), P^T 256-319 (fp16 pairs), dS^T 320-383 (fp16
@@ -57,12 +58,14 @@
 namespace fa {
 namespace bwd {
 
-constexpr int kThreads = 352;
+constexpr int kThreads = 480;
 constexpr int kQSlots = 2;
 constexpr int kComputeWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kReduceWarp = 10;  // issues the bulk dQ reductions
+constexpr int kDqWarp0 = 11;     // warps 11-14 read and stage dQ_i, one per TMEM lane quadrant
+constexpr int kDqWarps = 4;
 
 constexpr uint32_t kSmK = 0;
 constexpr uint32_t kSmV = kSmK + kTileBytes;
@@ -83,7 +86,7 @@ struct Ctl {
   uint64_t kv_full;
   uint64_t q_full[kQSlots], q_empty[kQSlots];
   uint64_t s_full, s_free, dp_full, p_full, dq_full, dq_free;
-  uint64_t dqs_full, dqs_free;  // dQ staging written by the 8 compute warps / read by the reduction
+  uint64_t dqs_full, dqs_free;  // dQ staging written by the 4 dQ warps / read by the reduction
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -156,8 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&ctl->s_free), kComputeWarps);
     mbar_init(smem_u32(&ctl->p_full), kComputeWarps);
     mbar_init(smem_u32(&ctl->dq_full), 1);
-    mbar_init(smem_u32(&ctl->dq_free), kComputeWarps);
-    mbar_init(smem_u32(&ctl->dqs_full), kComputeWarps);
+    mbar_init(smem_u32(&ctl->dq_free), kDqWarps);
+    mbar_init(smem_u32(&ctl->dqs_full), kDqWarps);
     mbar_init(smem_u32(&ctl->dqs_free), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
@@ -312,13 +315,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     // every reduction lands before the block exits
     if (lane == 0) bulk_wait_group0();
     __syncwarp();
+  } else if (warp >= kDqWarp0) {
+    // ------------------------------------------------------------ dQ_i readout
+    // lane = query row of the tile; each warp reads its lane quadrant's 64
+    // fp32 dQ columns and stages them for the reduction
+    const int quad = warp % 4;
+    const int r = quad * 32 + lane;
+    const uint32_t t_dq = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kColDP;
+    auto wait = [&](uint32_t bar, uint32_t parity) {
+      return mbar_wait_warp(bar, parity, abort_flag, p.status, kStatusTimeoutSoftmax,
+                            p.limit_ns);
+    };
+    for (int it = 0; it < n_steps; ++it) {
+      if (!wait(smem_u32(&ctl->dq_full), it & 1)) break;
+      tc_fence_after();
+      uint32_t dq[2][32];
+      tmem_ld32(t_dq, dq[0]);
+      tmem_ld32(t_dq + 32, dq[1]);
+      tc_wait_ld32(dq[0]);
+      tc_wait_ld32(dq[1]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));  // TMEM columns free for dP^T
+      // the staging buffer is rewritten once the previous reduction has read it
+      if (it > 0 && !wait(smem_u32(&ctl->dqs_free), (it - 1) & 1)) break;
+      // row r: 64 floats = 16 chunks of 16 B in two halves; chunk c of a half
+      // sits at position c ^ (r & 7) of that half (the accumulator keeps that
+      // order; eight consecutive rows hit eight different bank groups)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t srow = base + kSmDQ + r * 256 + h * 128;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(srow + ((e ^ (r & 7)) << 4)),
+                       "r"(dq[h][4 * e]), "r"(dq[h][4 * e + 1]), "r"(dq[h][4 * e + 2]),
+                       "r"(dq[h][4 * e + 3])
+                       : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->dqs_full));
+    }
   } else {
     // ------------------------------------------------------------ compute
     const int quad = warp % 4, half = warp / 4;  // lane quadrant, query-column half
     const int r = quad * 32 + lane;  // TMEM lane: key row, then query row of dQ
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t t_s = tmem + lane_base + kColS, t_dp = tmem + lane_base + kColDP;
-    const uint32_t t_dq = t_dp;  // dQ_i is written over dP^T
     const uint32_t t_p = tmem + lane_base + kColP, t_ds = tmem + lane_base + kColDS;
     const int key = j * 128 + r;
     const float c = p.scale_log2;
@@ -430,32 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- exponentials of the next tile while the tensor cores run this one's
       // dV, dK, dQ
       if (it + 1 < n_steps && !phase_p(it + 1)) { ok = false; break; }
-      // ---- dQ_i (lane = query row) into the fp32 accumulator
+      // this tile's dV, dK, dQ MMAs have read P^T and dS^T (TMEM and shared
+      // memory) before the next tile's are written
       if (!wait(smem_u32(&ctl->dq_full), it & 1)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t dq[32];
-      tmem_ld32(t_dq + 32 * half, dq);  // this warp's 32 of the 64 dQ columns
-      tc_wait_ld32(dq);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl->dq_free));  // TMEM columns free for dP^T
-      // the staging buffer is rewritten once the previous reduction has read it
-      if (it > 0 && !wait(smem_u32(&ctl->dqs_free), (it - 1) & 1)) { ok = false; break; }
-      // row r: 64 floats = 16 chunks of 16 B; this warp owns chunks 8 half ..
-      // 8 half + 7 and stores chunk c at position c ^ (r & 7) of its half (the
-      // accumulator keeps that order; eight consecutive rows hit eight
-      // different bank groups)
-      const uint32_t srow = base + kSmDQ + r * 256 + half * 128;
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(srow + ((e ^ (r & 7)) << 4)),
-                     "r"(dq[4 * e]), "r"(dq[4 * e + 1]), "r"(dq[4 * e + 2]), "r"(dq[4 * e + 3])
-                     : "memory");
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl->dqs_full));
     }
-    // ---- dK_j, dV_j (lane = key row): after the last dQ, every MMA is done.
+    // ---- dK_j, dV_j (lane = key row): after the last dQ_i signal, every MMA is done.
     // The TMEM loads are warp-collective: every lane takes part, only the
     // lanes of keys below n store.
     if (ok) {
