@@ -6,7 +6,8 @@ iterations between CUDA events, median / p10 / p90 per call).
 Added columns: TFLOPS (4*B*H*Nq*Nk*D, halved for causal) and the fraction of
 the measured B200 peak.  Added modes: ``--gpus N`` splits the (batch, head)
 slices over N devices of this process and reports the slowest device's time;
-``--sustained S`` runs each kernel back to back for S seconds while
+``--sustained S`` runs each kernel (forward, or backward with ``--backward``)
+back to back for S seconds while
 nvidia-smi samples device 0's SM clock and power, and reports the sustained
 TFLOPS with the median clock, the median power and TFLOPS per GHz (the
 per-clock efficiency, which is what decides throughput once a long run sits
@@ -200,6 +201,15 @@ def main(argv=None) -> None:
             print(f"{name:10s} unsupported for this dtype / head dimension")
             continue
         ops = [(dev, mk(dq, dk, dv)) for dev, dq, dk, dv in shards]
+        if args.backward and args.sustained > 0:
+            # autograd needs grad mode: no inference_mode here
+            ms, mhz, watts, reasons = sustained(ops, args.sustained)
+            tf = flops / (ms / 1e3) / 1e12
+            per_ghz = tf / (mhz / 1e3) if mhz else float("nan")
+            print(f"{name:10s} sustained {args.sustained:.0f} s (backward): {ms:.4f} ms/call, "
+                  f"{tf:.1f} TFLOPS, SM {mhz} MHz (median), {watts} W (median), "
+                  f"{per_ghz:.1f} TFLOPS/GHz, clock event reasons {reasons}")
+            continue
         if args.backward:
             # autograd needs grad mode; time the ops outside inference_mode
             ms = time_on_devices(ops, args.samples, args.iterations, args.warmup)

@@ -35,3 +35,11 @@ def test_cli_backward_mode(capsys):
                             "--kernels", "sm100", "sdpa", "--backward"])
     out = capsys.readouterr().out
     assert "(backward)" in out and "sm100" in out
+
+
+@pytest.mark.gpu
+def test_cli_backward_sustained_mode(capsys):
+    benchmark_forward.main(["--batch", "1", "--heads", "4", "--query-length", "1024",
+                            "--kernels", "sm100", "--backward", "--sustained", "1"])
+    out = capsys.readouterr().out
+    assert "sustained" in out and "(backward)" in out and "TFLOPS/GHz" in out
