@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* gen_base = smem_raw + (base - raw);
   Ctl* ctl = reinterpret_cast<Ctl*>(gen_base + kSmCtl);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // heaviest blocks (small j under the causal mask) first
+  // head-major: the key-tile blocks of one head run together and share its Q,
+  // dO and dQ tiles in L2
   const int bh = blockIdx.x / p.n_kt;
   const int j = blockIdx.x % p.n_kt;
   const int i0 = first_qtile(p, j);
