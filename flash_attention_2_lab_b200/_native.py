@@ -24,6 +24,8 @@ ABI = {
     "fa_fwd_sm100_varlen": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _f32, _vp]),
     "fa_fwd_sm100_noalloc": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _f32, _vp]),
     "fa_fwd_sm100_lse": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _f32, _vp]),
+    "fa_bwd_sm100_varlen": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                   _i64, _int, _f32, _vp]),
     "fa_bwd_sm100": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int,
                             _f32, _vp]),
     "fa_last_error": (ctypes.c_char_p, []),

@@ -2,9 +2,11 @@
 
 ``attention(q, k, v, causal=False, scale=None)`` runs the forward that also
 returns the row log-sum-exp (``fa_fwd_sm100_lse``) and, on backward, the
-backward kernel (``fa_bwd_sm100``): dQ, dK, dV in fp16 from one pass over the
-key tiles with P recomputed from the saved statistics.  q, k, v: contiguous
-fp16 CUDA tensors [B, H, N, 64] with equal query and key lengths.
+backward kernel (``fa_bwd_sm100_varlen``): dQ, dK, dV in fp16 from one pass
+over the key tiles with P recomputed from the saved statistics.  q: contiguous
+fp16 CUDA tensor [B, H, Nq, 64]; k, v: [B, H, Nk, 64] (Nk may differ from Nq;
+the causal mask is top-left, key j hidden from query i < j, as in the
+forward).
 
 The reference has no backward (its kernels are forward only); this is the
 training half of the same operator.
@@ -41,7 +43,7 @@ def attention(query, key, value, causal: bool = False, scale: float | None = Non
 
 
 def attention_forward_lse(query, key, value, causal: bool = False, scale: float | None = None):
-    """(output, row log-sum-exp [B, H, N] fp32)."""
+    """(output, row log-sum-exp [B, H, Nq] fp32)."""
     return tuple(ext().attention_forward_lse(query, key, value, causal, scale))
 
 

@@ -94,16 +94,18 @@ struct Ctl {
 static_assert(sizeof(Ctl) <= 256, "control block too large");
 
 struct Params {
-  int n;             // query and key rows per (batch, head)
-  int n_pad;         // n rounded up to 128 (rows of the row-term and dQ buffers)
+  int n_q;           // query rows per (batch, head)
+  int n_k;           // key rows per (batch, head)
+  int nq_pad;        // n_q rounded up to 128 (rows of the row-term and dQ buffers)
   int bh;
-  int causal;
-  int n_kt;          // key (and query) tiles per (batch, head)
+  int causal;        // top-left: key k is seen by queries q >= k
+  int n_kt;          // key tiles with at least one query per (batch, head): one block each
+  int n_qt;          // query tiles per (batch, head)
   float scale;       // softmax scale
   float scale_log2;  // scale * log2(e)
-  const float* rowterm;   // [bh][n_pad / 128][2][128]: per query tile L log2 e, then D
-  float* dq_acc;          // [bh][n_pad][64] fp32, zeroed before the launch
-  __half* dk;             // [bh][n][64]
+  const float* rowterm;   // [bh][nq_pad / 128][2][128]: per query tile L log2 e, then D
+  float* dq_acc;          // [bh][nq_pad][64] fp32, zeroed before the launch
+  __half* dk;             // [bh][n_k][64]
   __half* dv;
   unsigned int* status;
   unsigned long long limit_ns;
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bh = blockIdx.x / p.n_kt;
   const int j = blockIdx.x % p.n_kt;
   const int i0 = first_qtile(p, j);
-  const int n_steps = p.n_kt - i0;
+  const int n_steps = p.n_qt - i0;
   volatile int* abort_flag = &ctl->abort;
   auto qtile = [&](int it) { return i0 + it; };
 
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(base + kSmQ + slot * kTileBytes, &tm_q, full, 0, i * 128, bh);
         tma_load_3d(base + kSmDO + slot * kTileBytes, &tm_do, full, 0, i * 128, bh);
         bulk_load(base + kSmVec + slot * kVecBytes,
-                  p.rowterm + (static_cast<size_t>(bh) * p.n_pad + i * 128) * 2, kVecBytes, full);
+                  p.rowterm + (static_cast<size_t>(bh) * p.nq_pad + i * 128) * 2, kVecBytes, full);
       }
       __syncwarp();
       issued = it + 1;
@@ -305,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           kStatusTimeoutSoftmax, p.limit_ns))
         break;
       if (lane == 0) {
-        bulk_reduce_add_f32(p.dq_acc + (static_cast<size_t>(bh) * p.n_pad + qtile(it) * 128) * 64,
+        bulk_reduce_add_f32(p.dq_acc + (static_cast<size_t>(bh) * p.nq_pad + qtile(it) * 128) * 64,
                             base + kSmDQ, kDQBytes);
         bulk_commit_group();
         bulk_wait_group_read0();  // the staging buffer has been read
@@ -372,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // keys past n and (causal) queries before this key contribute nothing
     const int q_lo = p.causal ? key : 0;  // first query that sees this key
-    const bool key_ok = key < p.n;
+    const bool key_ok = key < p.n_k;
     const int key_max = j * 128 + quad * 32 + 31;  // last key of this warp
     // p of this warp's 64 queries of tile it, fp16 pairs: pk[16 c + u / 2]
     // holds queries 32 (2 half + c) + u, + 1
@@ -387,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // masks only where this warp's 32 keys x 64 queries reach past n or
       // (causal) below the diagonal
       const int q_min = i * 128 + 64 * half;
-      const bool masked = key_max >= p.n || q_min + 63 >= p.n || (p.causal && q_min < key_max);
+      const bool masked = key_max >= p.n_k || q_min + 63 >= p.n_q || (p.causal && q_min < key_max);
       auto exps = [&](auto mask_tag) {
         constexpr bool kMask = decltype(mask_tag)::value;
 #pragma unroll
@@ -407,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               pv[e] = ex2_approx(__uint_as_float(sr[u + e]) * c - lq[e]);
               if (kMask) {
                 const int q = i * 128 + ql + e;
-                if (!key_ok || q < q_lo || q >= p.n) pv[e] = 0.f;
+                if (!key_ok || q < q_lo || q >= p.n_q) pv[e] = 0.f;
               }
             }
             pk[16 * c2 + u / 2] = pack_half2(pv[0], pv[1]);
@@ -482,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The TMEM loads are warp-collective: every lane takes part, only the
     // lanes of keys below n store.
     if (ok) {
-      const size_t row = static_cast<size_t>(bh) * p.n + (key < p.n ? key : 0);
+      const size_t row = static_cast<size_t>(bh) * p.n_k + (key < p.n_k ? key : 0);
       {
         const int which = half;  // half 0 writes dV, half 1 dK
         const uint32_t col = which ? kColDK : kColDV;
@@ -498,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 16; ++e)
             hv[e] = pack_half2(__uint_as_float(g[2 * e]) * mul, __uint_as_float(g[2 * e + 1]) * mul);
           uint4* o4 = reinterpret_cast<uint4*>(out + 32 * h);
-          if (key < p.n) {
+          if (key < p.n_k) {
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               o4[e] = make_uint4(hv[4 * e], hv[4 * e + 1], hv[4 * e + 2], hv[4 * e + 3]);

@@ -50,6 +50,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <atomic>
 #include <map>
 #include <memory>
@@ -1448,22 +1449,28 @@ int fa_fwd_sm100_lse(const void* q, const void* k, const void* v, void* o, float
                 static_cast<cudaStream_t>(cuda_stream), nullptr, false, lse);
 }
 
-int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, const void* d_o,
-                 const float* lse, void* dq, void* dk, void* dv, int64_t batch, int64_t heads,
-                 int64_t seq_len, int causal, float scale, void* cuda_stream) {
-  if (batch < 0 || heads < 0 || seq_len < 0) return set_error(FA_ERR_INVALID, "negative size");
-  const int64_t bh = batch * heads, n = seq_len;
-  if (bh == 0 || n == 0) return FA_OK;
+int fa_bwd_sm100_varlen(const void* q, const void* k, const void* v, const void* o,
+                        const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                        int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int causal,
+                        float scale, void* cuda_stream) {
+  if (batch < 0 || heads < 0 || q_len < 0 || kv_len < 0)
+    return set_error(FA_ERR_INVALID, "negative size");
+  const int64_t bh = batch * heads, nq = q_len, nk = kv_len;
+  if (bh == 0 || (nq == 0 && nk == 0)) return FA_OK;
   const void* ptrs[] = {q, k, v, o, d_o, lse, dq, dk, dv};
   for (const void* ptr : ptrs) {
     if (ptr == nullptr) return set_error(FA_ERR_INVALID, "null pointer");
     if (reinterpret_cast<uintptr_t>(ptr) & 15)
       return set_error(FA_ERR_INVALID, "tensors must be 16-byte aligned");
   }
-  if (n > (1ll << 30) || bh > (1ll << 30)) return set_error(FA_ERR_INVALID, "size too large");
+  if (nq > (1ll << 30) || nk > (1ll << 30) || bh > (1ll << 30))
+    return set_error(FA_ERR_INVALID, "size too large");
   if (!(scale > 0.f) || !std::isfinite(scale))
     return set_error(FA_ERR_INVALID, "scale must be positive and finite");
-  const int64_t n_kt = (n + 127) / 128, n_pad = n_kt * 128;
+  if (nk == 0) return set_error(FA_ERR_INVALID, "key length must be positive when queries exist");
+  const int64_t n_qt = (nq + 127) / 128, nq_pad = n_qt * 128;
+  // causal (top-left): key tiles past the last query tile are seen by no query
+  const int64_t n_kt_all = (nk + 127) / 128, n_kt = causal ? std::min(n_kt_all, n_qt) : n_kt_all;
   if (bh * n_kt > 0x7fffffffll) return set_error(FA_ERR_INVALID, "too many blocks");
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   int dev = 0;
@@ -1472,10 +1479,17 @@ int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, con
   DeviceState* d = nullptr;
   int rc = ensure_device(dev, &d);
   if (rc != FA_OK) return rc;
+  if (nq == 0) {  // no queries: dK = dV = 0
+    const size_t bytes = static_cast<size_t>(bh) * nk * 64 * sizeof(__half);
+    if ((e = cudaMemsetAsync(dk, 0, bytes, stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(dv, 0, bytes, stream)) != cudaSuccess)
+      return set_error(FA_ERR_CUDA, "dK/dV clear: %s", cudaGetErrorString(e));
+    return FA_OK;
+  }
 
   // scratch: [counter prefix of the split mode, left alone][row terms][dQ accumulator]
-  const size_t rowterm_bytes = align256(static_cast<size_t>(bh) * n_pad * 2 * sizeof(float));
-  const size_t dq_bytes = static_cast<size_t>(bh) * n_pad * 64 * sizeof(float);
+  const size_t rowterm_bytes = align256(static_cast<size_t>(bh) * nq_pad * 2 * sizeof(float));
+  const size_t dq_bytes = static_cast<size_t>(bh) * nq_pad * 64 * sizeof(float);
   void* ws = nullptr;
   if ((rc = get_workspace(dev, stream, kCounterBytes + rowterm_bytes + dq_bytes, &ws)) != FA_OK)
     return rc;
@@ -1484,25 +1498,36 @@ int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, con
   float* dq_acc = reinterpret_cast<float*>(wb + rowterm_bytes);
   e = cudaMemsetAsync(dq_acc, 0, dq_bytes, stream);
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "dQ clear: %s", cudaGetErrorString(e));
+  if (n_kt * 128 < nk) {  // dK = dV = 0 for the keys of those tiles
+    const size_t pitch = static_cast<size_t>(nk) * 64 * sizeof(__half);
+    const size_t skip = static_cast<size_t>(n_kt) * 128 * 64 * sizeof(__half);
+    if ((e = cudaMemset2DAsync(static_cast<uint8_t*>(dk) + skip, pitch, 0, pitch - skip, bh,
+                               stream)) != cudaSuccess ||
+        (e = cudaMemset2DAsync(static_cast<uint8_t*>(dv) + skip, pitch, 0, pitch - skip, bh,
+                               stream)) != cudaSuccess)
+      return set_error(FA_ERR_CUDA, "dK/dV clear: %s", cudaGetErrorString(e));
+  }
 
-  const int64_t rows_pad = bh * n_pad;
+  const int64_t rows_pad = bh * nq_pad;
   fa::bwd::rowterm_kernel<<<static_cast<unsigned>((rows_pad + 255) / 256), 256, 0, stream>>>(
       static_cast<const __half*>(o), static_cast<const __half*>(d_o), lse, rowterm,
-      static_cast<int>(n), static_cast<int>(n_pad), rows_pad);
+      static_cast<int>(nq), static_cast<int>(nq_pad), rows_pad);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
 
   CUtensorMap tq, tk, tv, tdo;
-  if ((rc = make_map(&tq, q, n, bh, 128)) != FA_OK) return rc;
-  if ((rc = make_map(&tk, k, n, bh, 128)) != FA_OK) return rc;
-  if ((rc = make_map(&tv, v, n, bh, 128)) != FA_OK) return rc;
-  if ((rc = make_map(&tdo, d_o, n, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tq, q, nq, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tk, k, nk, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tv, v, nk, bh, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tdo, d_o, nq, bh, 128)) != FA_OK) return rc;
   fa::bwd::Params bp;
-  bp.n = static_cast<int>(n);
-  bp.n_pad = static_cast<int>(n_pad);
+  bp.n_q = static_cast<int>(nq);
+  bp.n_k = static_cast<int>(nk);
+  bp.nq_pad = static_cast<int>(nq_pad);
   bp.bh = static_cast<int>(bh);
   bp.causal = causal ? 1 : 0;
   bp.n_kt = static_cast<int>(n_kt);
+  bp.n_qt = static_cast<int>(n_qt);
   bp.scale = scale;
   bp.scale_log2 = scale * 1.4426950408889634f;
   bp.rowterm = rowterm;
@@ -1516,12 +1541,20 @@ int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, con
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
 
-  const int64_t rows = bh * n;
+  const int64_t rows = bh * nq;
   fa::bwd::dq_convert_kernel<<<static_cast<unsigned>((rows * 8 + 255) / 256), 256, 0, stream>>>(
-      dq_acc, static_cast<__half*>(dq), static_cast<int>(n), static_cast<int>(n_pad), rows, scale);
+      dq_acc, static_cast<__half*>(dq), static_cast<int>(nq), static_cast<int>(nq_pad), rows,
+      scale);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   return FA_OK;
+}
+
+int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                 const float* lse, void* dq, void* dk, void* dv, int64_t batch, int64_t heads,
+                 int64_t seq_len, int causal, float scale, void* cuda_stream) {
+  return fa_bwd_sm100_varlen(q, k, v, o, d_o, lse, dq, dk, dv, batch, heads, seq_len, seq_len,
+                             causal, scale, cuda_stream);
 }
 
 int fa_fwd_sm100_debug(const void* q, const void* k, const void* v, void* o, int64_t batch,

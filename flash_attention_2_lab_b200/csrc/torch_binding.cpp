@@ -146,39 +146,55 @@ torch::Tensor attention_forward(torch::Tensor query, torch::Tensor key, torch::T
 
 namespace {
 
-void check_training_inputs(const std::vector<std::pair<const char*, const torch::Tensor*>>& ts,
-                           const torch::Tensor& ref) {
-  for (const auto& nt : ts) {
-    const torch::Tensor& t = *nt.second;
-    TORCH_CHECK(t.is_cuda(), nt.first, " must be a CUDA tensor");
-    TORCH_CHECK(t.device() == ref.device(), nt.first, " must be on the same device as query");
-    TORCH_CHECK(t.scalar_type() == at::kHalf, nt.first, " must have dtype torch.float16");
-    TORCH_CHECK(t.sizes() == ref.sizes(), nt.first, " must have the shape of query");
-    TORCH_CHECK(t.is_contiguous(), nt.first, " must be contiguous");
-  }
+// Tensors shaped like query [B, H, Nq, 64] (query, output, grad_output) and
+// like key [B, H, Nk, 64] (key, value).
+void check_training_inputs(const std::vector<std::pair<const char*, const torch::Tensor*>>& qs,
+                           const std::vector<std::pair<const char*, const torch::Tensor*>>& ks) {
+  const torch::Tensor& ref = *qs.front().second;
   TORCH_CHECK(ref.dim() == 4, "query must have shape [B, H, N, D]");
   TORCH_CHECK(ref.size(3) == kHeadDimension, "head dimension must equal 64");
+  auto common = [&](const char* name, const torch::Tensor& t) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(t.device() == ref.device(), name, " must be on the same device as query");
+    TORCH_CHECK(t.scalar_type() == at::kHalf, name, " must have dtype torch.float16");
+    TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  };
+  for (const auto& nt : qs) {
+    common(nt.first, *nt.second);
+    TORCH_CHECK(nt.second->sizes() == ref.sizes(), nt.first, " must have the shape of query");
+  }
+  const torch::Tensor& kref = *ks.front().second;
+  for (const auto& nt : ks) {
+    const torch::Tensor& t = *nt.second;
+    common(nt.first, t);
+    TORCH_CHECK(t.dim() == 4 && t.size(0) == ref.size(0) && t.size(1) == ref.size(1) &&
+                    t.size(3) == kHeadDimension,
+                nt.first, " must have shape [B, H, N_kv, 64] with query's B and H");
+    TORCH_CHECK(t.sizes() == kref.sizes(), nt.first, " must have the shape of key");
+  }
 }
 
 }  // namespace
 
-// Forward that also returns the row log-sum-exp [B, H, N] (fp32) for the
-// backward; equal query and key lengths.  No counterpart in the reference.
+// Forward that also returns the row log-sum-exp [B, H, Nq] (fp32) for the
+// backward; key length may differ from the query length.  No counterpart in
+// the reference.
 std::vector<torch::Tensor> attention_forward_lse(torch::Tensor query, torch::Tensor key,
                                                  torch::Tensor value, bool causal,
                                                  std::optional<double> scale) {
-  check_training_inputs({{"query", &query}, {"key", &key}, {"value", &value}}, query);
+  check_training_inputs({{"query", &query}}, {{"key", &key}, {"value", &value}});
   const c10::cuda::CUDAGuard device_guard(query.device());
   torch::Tensor output = torch::empty_like(query);
   torch::Tensor lse = torch::empty({query.size(0), query.size(1), query.size(2)},
                                    query.options().dtype(at::kFloat));
-  const int64_t batch = query.size(0), heads = query.size(1), n = query.size(2);
-  if (batch == 0 || heads == 0 || n == 0) return {output, lse};
+  const int64_t batch = query.size(0), heads = query.size(1), nq = query.size(2),
+                nk = key.size(2);
+  if (batch == 0 || heads == 0 || nq == 0) return {output, lse};
   const float s = scale.has_value() ? static_cast<float>(*scale)
                                     : 1.0f / std::sqrt(static_cast<float>(kHeadDimension));
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(query.get_device()).stream();
   check_status(fa_fwd_sm100_lse(query.data_ptr(), key.data_ptr(), value.data_ptr(),
-                                output.data_ptr(), lse.data_ptr<float>(), batch, heads, n, n,
+                                output.data_ptr(), lse.data_ptr<float>(), batch, heads, nq, nk,
                                 causal ? 1 : 0, s, stream));
   return {output, lse};
 }
@@ -189,26 +205,27 @@ std::vector<torch::Tensor> attention_backward(torch::Tensor query, torch::Tensor
                                               torch::Tensor value, torch::Tensor output,
                                               torch::Tensor grad_output, torch::Tensor lse,
                                               bool causal, std::optional<double> scale) {
-  check_training_inputs({{"query", &query}, {"key", &key}, {"value", &value}, {"output", &output},
-                         {"grad_output", &grad_output}},
-                        query);
+  check_training_inputs({{"query", &query}, {"output", &output}, {"grad_output", &grad_output}},
+                        {{"key", &key}, {"value", &value}});
   TORCH_CHECK(lse.is_cuda() && lse.device() == query.device(), "lse must be on query's device");
   TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.dim() == 3 &&
                   lse.size(0) == query.size(0) && lse.size(1) == query.size(1) &&
                   lse.size(2) == query.size(2),
-              "lse must be a contiguous float32 tensor of shape [B, H, N]");
+              "lse must be a contiguous float32 tensor of shape [B, H, N_q]");
   const c10::cuda::CUDAGuard device_guard(query.device());
   torch::Tensor dq = torch::empty_like(query), dk = torch::empty_like(key),
                 dv = torch::empty_like(value);
-  const int64_t batch = query.size(0), heads = query.size(1), n = query.size(2);
-  if (batch == 0 || heads == 0 || n == 0) return {dq, dk, dv};
+  const int64_t batch = query.size(0), heads = query.size(1), nq = query.size(2),
+                nk = key.size(2);
+  if (batch == 0 || heads == 0 || (nq == 0 && nk == 0)) return {dq, dk, dv};
   const float s = scale.has_value() ? static_cast<float>(*scale)
                                     : 1.0f / std::sqrt(static_cast<float>(kHeadDimension));
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(query.get_device()).stream();
-  check_status(fa_bwd_sm100(query.data_ptr(), key.data_ptr(), value.data_ptr(),
-                            output.data_ptr(), grad_output.data_ptr(), lse.data_ptr<float>(),
-                            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), batch, heads, n,
-                            causal ? 1 : 0, s, stream));
+  check_status(fa_bwd_sm100_varlen(query.data_ptr(), key.data_ptr(), value.data_ptr(),
+                                   output.data_ptr(), grad_output.data_ptr(),
+                                   lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(),
+                                   dv.data_ptr(), batch, heads, nq, nk, causal ? 1 : 0, s,
+                                   stream));
   return {dq, dk, dv};
 }
 

@@ -88,18 +88,28 @@ int fa_fwd_sm100_lse(const void* q, const void* k, const void* v, void* o, float
                      float scale, void* cuda_stream);
 
 /*
- * Attention backward, head dimension 64, equal query and key lengths:
- * given q, k, v, the forward output o, the output gradient d_o (all fp16
- * [batch, heads, seq_len, 64]) and the forward's lse (fp32 [batch, heads,
- * seq_len], from fa_fwd_sm100_lse), writes dq, dk, dv (fp16, same layout):
- *   P = exp(scale * Q K^T - lse) (causal: key > query masked),
+ * Attention backward, head dimension 64: given q (fp16 [batch, heads, q_len,
+ * 64]), k, v (fp16 [batch, heads, kv_len, 64]), the forward output o and the
+ * output gradient d_o (fp16, q's shape) and the forward's lse (fp32 [batch,
+ * heads, q_len], from fa_fwd_sm100_lse), writes dq (q's shape) and dk, dv
+ * (k's shape):
+ *   P = exp(scale * Q K^T - lse) (causal: top-left, key j > query i masked,
+ *       as in the forward),
  *   dV = P^T dO,  dP = dO V^T,  dS = P * (dP - rowsum(dO * O)),
  *   dQ = scale * dS K,  dK = scale * dS^T Q.
+ * Keys that no query sees (causal with kv_len > q_len) get dK = dV = 0.
+ * kv_len = 0 with q_len > 0 is rejected, as in the forward.
  * Uses the scratch buffer per (device, stream) of the split mode for the
  * fp32 dQ accumulator and the row terms (allocated or grown on first need,
  * so the first call on a stream allocates).
  * No counterpart in the reference (it has no backward).
  */
+int fa_bwd_sm100_varlen(const void* q, const void* k, const void* v, const void* o,
+                        const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                        int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int causal,
+                        float scale, void* cuda_stream);
+
+/* fa_bwd_sm100_varlen with q_len = kv_len = seq_len. */
 int fa_bwd_sm100(const void* q, const void* k, const void* v, const void* o, const void* d_o,
                  const float* lse, void* dq, void* dk, void* dv, int64_t batch, int64_t heads,
                  int64_t seq_len, int causal, float scale, void* cuda_stream);

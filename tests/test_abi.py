@@ -152,6 +152,12 @@ def test_training_entry_points_validate_without_gpu():
     assert lib.fa_bwd_sm100(None, None, None, None, None, None, None, None, None, 1, 1, 128, 0,
                             0.125, None) == -1
     assert "null" in _native.last_error()
+    args9 = [None] * 9
+    assert lib.fa_bwd_sm100_varlen(*args9, 1, 1, -1, 128, 0, 0.125, None) == -1
+    assert "negative" in _native.last_error()
+    assert lib.fa_bwd_sm100_varlen(*args9, 0, 1, 128, 256, 0, 0.125, None) == 0
+    assert lib.fa_bwd_sm100_varlen(*args9, 1, 1, 128, 256, 0, 0.125, None) == -1
+    assert "null" in _native.last_error()
     assert lib.fa_fwd_sm100_lse(16, 16, 16, 16, None, 1, 1, 128, 128, 0, 0.125, None) == -1
     ext = _native.ext()
     x = torch.zeros(1, 1, 128, 64, dtype=torch.float16)
