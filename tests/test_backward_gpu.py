@@ -181,3 +181,22 @@ def test_autograd_function_unequal_lengths():
         grad_close(qs.grad, dq_ref, "dq")
         grad_close(ks.grad, dk_ref, "dk")
         grad_close(vs.grad, dv_ref, "dv")
+
+
+def test_training_binding_shape_checks():
+    ext = _native.ext()
+    q = torch.randn(1, 2, 128, 64, device="cuda").half()
+    k = torch.randn(1, 2, 256, 64, device="cuda").half()
+    o, lse = ext.attention_forward_lse(q, k, k, False, None)
+    assert o.shape == q.shape and lse.shape == (1, 2, 128)
+    with pytest.raises(RuntimeError, match="key must have shape"):
+        ext.attention_forward_lse(q, torch.randn(2, 2, 256, 64, device="cuda").half(), k, False,
+                                  None)
+    with pytest.raises(RuntimeError, match="value must have the shape of key"):
+        ext.attention_forward_lse(q, k, torch.randn(1, 2, 128, 64, device="cuda").half(), False,
+                                  None)
+    with pytest.raises(RuntimeError, match="grad_output must have the shape of query"):
+        ext.attention_backward(q, k, k, o, torch.randn(1, 2, 256, 64, device="cuda").half(), lse,
+                               False, None)
+    with pytest.raises(RuntimeError, match="lse must be"):
+        ext.attention_backward(q, k, k, o, o, lse[:, :, :64].contiguous(), False, None)
