@@ -9,8 +9,12 @@
 //   dV = P^T dO,   dP = dO V^T,   dS = P * (dP - D),   D = rowsum(dO * O)
 //   dK = scale * dS^T Q,          dQ = scale * dS K
 //
-// One block per (batch*head, 128-key tile j); it keeps K_j, V_j, dK_j and dV_j
-// on chip and walks the query tiles i (all of them, or i >= j when causal):
+// Query length n_q and key length n_k may differ (causal mask top-left: key
+// k is seen by queries q >= k, as in the forward).  One block per
+// (batch*head, 128-key tile j), head-major; it keeps K_j, V_j, dK_j and dV_j
+// on chip and walks the query tiles i (all of them, or i >= j when causal;
+// key tiles that no query reaches get no block, the host clears their dK,
+// dV):
 //
 //   warp 8   TMA producer: K_j, V_j once; per query tile Q_i, dO_i and the
 //            row terms (L * log2 e, D) into a two-slot ring.
