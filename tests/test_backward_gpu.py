@@ -63,7 +63,8 @@ def grad_close(got, ref, what):
     return worst
 
 
-CASES = [(1, 2, 128), (1, 2, 256), (2, 3, 384), (1, 4, 1024), (1, 2, 200), (2, 2, 1000)]
+CASES = [(1, 2, 128), (1, 2, 256), (2, 3, 384), (1, 4, 1024), (1, 2, 200), (2, 2, 1000),
+         (1, 2, 4096)]
 
 
 @pytest.mark.parametrize("causal", [False, True])
