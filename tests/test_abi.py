@@ -158,6 +158,15 @@ def test_training_entry_points_validate_without_gpu():
     assert lib.fa_bwd_sm100_varlen(*args9, 0, 1, 128, 256, 0, 0.125, None) == 0
     assert lib.fa_bwd_sm100_varlen(*args9, 1, 1, 128, 256, 0, 0.125, None) == -1
     assert "null" in _native.last_error()
+    aligned, odd = [4096] * 9, [4096] * 8 + [4104]
+    assert lib.fa_bwd_sm100_varlen(*odd, 1, 1, 128, 256, 0, 0.125, None) == -1
+    assert "16-byte aligned" in _native.last_error()
+    assert lib.fa_bwd_sm100_varlen(*aligned, 1, 1, 128, 256, 0, 0.0, None) == -1
+    assert "scale" in _native.last_error()
+    assert lib.fa_bwd_sm100_varlen(*aligned, 1, 1, 128, 0, 0, 0.125, None) == -1
+    assert "key length" in _native.last_error()
+    assert lib.fa_bwd_sm100_varlen(*aligned, 1, 1, 1 << 31, 128, 0, 0.125, None) == -1
+    assert "too large" in _native.last_error()
     assert lib.fa_fwd_sm100_lse(16, 16, 16, 16, None, 1, 1, 128, 128, 0, 0.125, None) == -1
     ext = _native.ext()
     x = torch.zeros(1, 1, 128, 64, dtype=torch.float16)
