@@ -114,7 +114,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 3-D tiled load (no multicast): coordinates are {inner (elements), row, slice}.
+// 3-D tiled load into this CTA's shared memory: coordinates are {inner (elements), row, slice}.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map,
                                             uint32_t bar, int c0, int c1, int c2) {
   asm volatile(
